@@ -1,0 +1,478 @@
+"""Benchmark: the batched Kokoro-82M decoder-stage op stream on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Headline workload: the ISTFTNet generator's elementwise /
+broadcast / reduction op stream for a batch of utterances (64 per GPU by
+default), features [512, 400] -> stages [256, 4000] and [128, 24001], conv
+and fc outputs as seeded stand-ins resident in HBM.  One step = the whole
+stream for the batch (49 kernel launches).  With torchrun (N > 1) every rank
+runs its own 64 utterances (utterance sharding, no collective on the data
+path; "scaling": "weak"), timing is the max over ranks.
+
+Printed (rank 0, one JSON line): utt/s over all ranks from CUDA events with
+inputs resident; ``e2e`` through FusedDecoder.run_host with pinned host
+buffers (features + fc outputs in, final stage output out, every step);
+``roofline`` for the dominant kernel (bt_adain_snake) from per-launch CUDA
+events; ``cpu_baseline`` = the numpy oracle on the host cores; ``per_op`` =
+each BASELINE op config c1-c4 (GB/s, fraction of the measured HBM peak and
+of the nominal 8 TB/s) plus a >= 256 MB sweep, each next to the oracle's
+single-core numpy time; ``clocks`` sampled with nvidia-smi during the timed
+region.  ``--impl reference`` times the oracle port (the reference's numpy
+op table, restated in oracle/) on the host cores instead.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+import warnings
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [REPO, os.path.join(REPO, "best-tts-godot_b200")]
+
+METRIC = "Kokoro decoder op-stream utt/s"
+UNIT = "utt/s"
+NOMINAL_HBM = 8000.0
+DATA = ("synthetic: seeded N(0,1) features, fc outputs (from N(0,1) style vectors through seeded "
+        "Linear(128->2C)) and conv-output stand-ins; seeded alpha ~ U(0.5,1.5)")
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def config(args, n):
+    from bt_b200.decoder import stage_shapes
+    return {"workload": "c5: batched Kokoro-82M ISTFTNet decoder-stage op stream (BASELINE configs[4])",
+            "batch_per_gpu": args.batch, "global_batch": args.batch * n, "t0": args.t0,
+            "stage_shapes": [[c, t] for (_, _, c, t) in stage_shapes(args.t0)],
+            "parallelism": f"utterance-sharded over {n} GPU(s), no collective on the data path",
+            "l2": "no flush needed: inputs larger than L2 (each stage-2 tensor is "
+                  f"{args.batch * 128 * (args.t0 * 60 + 1) * 4 / 1e6:.0f} MB)",
+            "launches_per_step": 49}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle (numpy op table) on the host cores
+# ---------------------------------------------------------------------------
+def _oracle_utterance(args):
+    t0, seed = args
+    sys.path[:0] = [REPO, os.path.join(REPO, "best-tts-godot_b200")]
+    import numpy as np  # noqa
+    from bt_b200.decoder import build_stream
+    from oracle import OracleRuntime, run_nodes_streaming
+    S = build_stream(1, t0=t0)
+    rng = np.random.default_rng(seed)
+    env = {name: rng.standard_normal(shape, dtype=np.float32) for name, (shape, dt, kind) in sorted(S.inputs.items())}
+    env.update(S.consts)
+    t = time.perf_counter()
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        run_nodes_streaming(OracleRuntime(), S.nodes, env, keep=[S.final])
+    return time.perf_counter() - t
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_pool(procs):
+    import multiprocessing as mp
+    return mp.get_context("spawn").Pool(procs)
+
+
+def oracle_step(pool, procs, t0, step):
+    """procs utterances, one per worker; returns (wall seconds, utterances)."""
+    t = time.perf_counter()
+    pool.map(_oracle_utterance, [(t0, 1000 * step + i) for i in range(procs)])
+    return time.perf_counter() - t, procs
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    n = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if rank != 0:
+        return 0
+    procs = max(1, min(cpu_cores(), args.cpu_procs))
+    pool = cpu_pool(procs)
+    for w in range(args.warmup):
+        oracle_step(pool, procs, args.t0, w)
+    tot, utts = 0.0, 0
+    for k in range(args.steps):
+        dt, u = oracle_step(pool, procs, args.t0, args.warmup + k)
+        tot += dt
+        utts += u
+    pool.close()
+    value = utts / tot
+    sample = (f"{procs} full-length utterances per step, one per worker process (numpy oracle, "
+              f"oracle/ops.py, the reference's op table restated), {args.steps} steps")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": n,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "config": config(args, n),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def read_profile_traffic():
+    """Per-launch DRAM traffic of the dominant kernel from the committed ncu
+    summary (profiles/adain_snake_c5.md, line 'traffic_bytes_per_launch: N'),
+    or None when no capture has been summarised."""
+    p = os.path.join(REPO, "profiles", "adain_snake_c5.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def adain_bytes(rows, cols, n_src, n_out, has_res):
+    """Algorithmic bytes of one bt_adain_snake launch: each source row read
+    once, the residual and every output written once (fp32); the per-row
+    parameters are included."""
+    n = rows * cols * 4
+    return n * (n_src + n_out + (1 if has_res else 0)) + rows * n_out * 8
+
+
+def measure_op(fn, bytes_, flush, reps, torch):
+    """Median CUDA-event time of fn() over reps, L2 flushed before each."""
+    import statistics
+    for _ in range(3):
+        fn()
+    times = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    return ms, bytes_ / (ms * 1e-3) / 1e9
+
+
+def per_op(rt, torch, peak):
+    """BASELINE configs c1-c4 and a >= 256 MB sweep (rank 0, N = 1)."""
+    from bt_b200 import configs
+    from oracle import OracleRuntime
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()   # noqa: E731
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")   # 256 MB > L2
+    res = {}
+
+    def entry(name, fn, nbytes, cpu_fn=None, reps=10):
+        ms, gbs = measure_op(fn, nbytes, flush, reps, torch)
+        e = {"ms": round(ms, 5), "bytes": int(nbytes), "GBps": round(gbs, 1),
+             "frac_of_measured": round(gbs / peak, 4), "frac_of_8TBps": round(gbs / NOMINAL_HBM, 4)}
+        if cpu_fn is not None:
+            with warnings.catch_warnings():
+                warnings.simplefilter("ignore")
+                t = time.perf_counter()
+                cpu_fn()
+                e["cpu_ms_1core"] = round(1e3 * (time.perf_counter() - t), 2)
+        res[name] = e
+
+    orc = OracleRuntime()
+
+    def onode(op, env, ins, at=None):
+        return lambda: orc.dispatch(op, ins, ["_o"], at or {}, dict(env))
+
+    c = configs.c1()
+    X, B = dev(c["X"]), dev(c["B"])
+    entry("c1_add", lambda: rt.elementwise("ADD", [X, B], X.shape, np.float32, np.float32), 4196352,
+          onode("Add", c, ["X", "B"]))
+    entry("c1_mul", lambda: rt.elementwise("MUL", [X, B], X.shape, np.float32, np.float32), 4196352,
+          onode("Mul", c, ["X", "B"]))
+    y = rt.elementwise("ADD", [X, B], X.shape, np.float32, np.float32)
+    yh = {"y": (c["X"] + c["B"]).astype(np.float32)}
+    for nm, op, onnx, at in [("c1_sigmoid", "SIGMOID", "Sigmoid", {}), ("c1_tanh", "TANH", "Tanh", {}),
+                             ("c1_leakyrelu", "LEAKYRELU", "LeakyRelu", {"alpha": 0.2})]:
+        entry(nm, lambda op=op: rt.elementwise(op, [y], y.shape, np.float32, np.float32, alpha=0.2), 4194304,
+              onode(onnx, yh, ["y"], at))
+    c = configs.c2_layernorm()
+    Xl, g, b = dev(c["X"]), dev(c["gamma"]), dev(c["beta"])
+    entry("c2_layernorm", lambda: rt.layernorm(Xl, None, None, g, b, -1, 1e-12), 3139584,
+          onode("LayerNormalization", {"X": c["X"], "g": c["gamma"], "b": c["beta"]}, ["X", "g", "b"],
+                {"epsilon": 1e-12}))
+    c = configs.c2_adain()
+    Xa, h = dev(c["X"]), dev(c["h"][:, :, 0])
+    Cc = c["X"].shape[1]
+    gain = rt.elementwise("ADD", [h[:, :Cc], dev(np.array(1.0, np.float16))], (1, Cc), np.float32, np.float32)
+    outa = [torch.empty_like(Xa)]
+    entry("c2_adain", lambda: rt.adain_snake([Xa], gain, h[:, Cc:], np.float32(c["eps"]), outs=outa), 8392704)
+    c = configs.c2_reducemean()
+    Xr = dev(c["X"])
+    entry("c2_reducemean", lambda: rt._reduce_block(Xr, [2], 1), 268566528,
+          onode("ReduceMean", {"X": c["X"], "ax": np.array([-1], np.int64)}, ["X", "ax"]))
+    del Xr
+    for bsz, nbytes in ((1, 24971640), (16, 399515640)):
+        c = configs.c3(batch=bsz)
+        Xs, M = dev(c["X"]), dev(c["mask"])
+        entry(f"c3_softmax_b{bsz}", lambda: rt.softmax(Xs, M, -1), nbytes,
+              lambda c=c: OracleRuntime().run_nodes([("Add", ["X", "mask"], ["s"], {}),
+                                                     ("Softmax", ["s"], ["y"], {})], dict(c)))
+        del Xs
+    for shape, nbytes in (((512, 512, 3), 3936256), ((256, 256, 7), 2295808)):
+        c = configs.c4_dequant(shape=shape)
+        W, s, z, gn = dev(c["W"]), dev(c["scale"]), dev(c["zp"]), dev(c["gain"])
+        entry(f"c4_dequant_{shape[0]}", lambda: rt.dequant_mul(W, s, z, gn), nbytes,
+              lambda c=c: OracleRuntime().run_nodes([("DequantizeLinear", ["W", "scale", "zp"], ["d"], {}),
+                                                     ("Mul", ["d", "gain"], ["y"], {})], dict(c)))
+    c = configs.c4_cast()
+    Xc = dev(c["X"])
+    entry("c4_cast", lambda: rt.elementwise("IDENTITY", [Xc], Xc.shape, np.float32, np.float64), 492000000,
+          onode("Cast", c, ["X"], {"to": 1}))
+    del Xc
+    # >= 256 MB sweep
+    n = 64 * 1024 * 1024
+    A = torch.randn((8192, 8192), device="cuda")
+    Bv = torch.randn((8192, 1), device="cuda")
+    sweep = {}
+    for nm, op, ins, nb in [("add_rowbcast", "ADD", [A, Bv], 2 * n * 4 + 8192 * 4), ("mul_same", "MUL", [A, A], 3 * n * 4),
+                            ("sigmoid", "SIGMOID", [A], 2 * n * 4), ("tanh", "TANH", [A], 2 * n * 4),
+                            ("leakyrelu", "LEAKYRELU", [A], 2 * n * 4), ("sin", "SIN", [A], 2 * n * 4),
+                            ("exp", "EXP", [A], 2 * n * 4)]:
+        ms, gbs = measure_op(lambda op=op, ins=ins: rt.elementwise(op, ins, A.shape, np.float32, np.float32,
+                                                                     alpha=0.2), nb, flush, 5, torch)
+        sweep[nm] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    gl = torch.rand(768, device="cuda")
+    Al = A.reshape(-1, 768)[: (n // 768)]
+    ms, gbs = measure_op(lambda: rt.layernorm(Al, None, None, gl, None, -1, 1e-5), 2 * Al.numel() * 4 + 3072,
+                         flush, 5, torch)
+    sweep["layernorm_768"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    A3 = A.reshape(64, 128, 8192)
+    gsw = torch.rand((64, 128), device="cuda")
+    osw = [torch.empty_like(A3)]
+    ms, gbs = measure_op(lambda: rt.adain_snake([A3], gsw, gsw, 1e-5, outs=osw), 2 * n * 4, flush, 5, torch)
+    sweep["adain_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    ms, gbs = measure_op(lambda: rt._reduce_block(A3, [2], 1), n * 4, flush, 5, torch)
+    sweep["reducemean_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    res["sweep_256MB"] = sweep
+    return res
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    from bt_b200.decoder import (FusedDecoder, build_stream, fill_conv_standins, host_inputs,
+                                 stream_algorithmic_bytes, stream_launches)
+    from bt_b200.runtime import BtRuntime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = world
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    peak, peak_kind = peaks()
+
+    # CPU baseline pool first (spawned workers; rank 0 at N = 1 only)
+    do_cpu = rank == 0 and n == 1 and not args.no_cpu_baseline
+    pool = None
+    if do_cpu:
+        procs = max(1, min(cpu_cores(), args.cpu_procs))
+        pool = cpu_pool(procs)
+
+    S = build_stream(args.batch, t0=args.t0)
+    dec = FusedDecoder(S, dev)
+    fill_conv_standins(dec, seed=17 + rank)
+    host = host_inputs(S, seed=100 + rank)
+    hin, hout = dec.host_buffers()
+    dec.fill_host(hin, host)
+    dec.run_host(hin, hout)             # inputs resident from here on
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return v
+
+    for _ in range(args.warmup):
+        dec.launch()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    record = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    launches = 0
+    for _ in range(args.steps):
+        launches += dec.launch(record=record)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    elapsed = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    value = n * args.batch * args.steps / elapsed
+    ms_step = 1e3 * elapsed / args.steps
+
+    # dominant kernel: bt_adain_snake launches of the timed region
+    ad_bytes = ad_time = 0.0
+    ad_n = 0
+    kind_time = {}
+    for kind, rows, cols, n_src, n_out, has_res, a, b in record:
+        t = a.elapsed_time(b) / 1e3
+        kind_time[kind] = kind_time.get(kind, 0.0) + t
+        if kind == "adain":
+            ad_bytes += adain_bytes(rows, cols, n_src, n_out, has_res)
+            ad_time += t
+            ad_n += 1
+    achieved = ad_bytes / ad_time / 1e9
+    traffic = read_profile_traffic()
+    roofline = {"bound": "hbm", "kernel": "bt_adain_snake (adain_snake_kernel)", "achieved": round(achieved, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "frac_of_8TBps": round(achieved / NOMINAL_HBM, 4), "peak_kind": peak_kind,
+                "traffic": traffic, "launches_timed": ad_n,
+                "algorithmic_bytes_per_launch": round(ad_bytes / max(ad_n, 1)),
+                "avg_launch_ms": round(1e3 * ad_time / max(ad_n, 1), 4),
+                "share_of_step_time": round(ad_time / max(sum(kind_time.values()), 1e-12), 4)}
+    stream_bytes = stream_algorithmic_bytes(S)
+
+    # end to end through the host-buffer API
+    for _ in range(args.warmup):
+        dec.run_host(hin, hout)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        h2d, d2h = dec.run_host(hin, hout)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(f0.elapsed_time(f1) / 1e3)
+    e2e = {"value": n * args.batch * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "ms_per_step": round(1e3 * e2e_s / args.steps, 3),
+           "api": "FusedDecoder.run_host (pinned host buffers, copies on the compute stream)"}
+
+    extra = {}
+    if rank == 0 and n == 1 and not args.no_per_op:
+        rt = BtRuntime(dev)
+        extra["per_op"] = per_op(rt, torch, peak)
+
+    cpu = None
+    if do_cpu:
+        procs = pool._processes
+        oracle_step(pool, procs, args.t0, 0)             # warm the workers (imports)
+        dt, u = oracle_step(pool, procs, args.t0, 1)
+        pool.close()
+        cpu = {"value": u / dt, "unit": UNIT, "cores": procs, "kind": "port",
+               "sample": f"{u} full-length utterances, one per worker process, through the numpy oracle "
+                         "(oracle/ops.py, the reference's op table restated), after one warm-up round"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": DATA, "config": config(args, n),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                "clocks": clk, "stream_algorithmic_bytes_per_step": stream_bytes,
+                "stream_GBps": round(stream_bytes * args.steps / elapsed / n / 1e9 * n, 1),
+                "stream_frac_of_measured": round(stream_bytes / (elapsed / args.steps) / 1e9 / peak, 4)}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="utterances per GPU")
+    ap.add_argument("--t0", type=int, default=400)
+    ap.add_argument("--cpu-procs", type=int, default=64)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-op", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,559 @@
+"""Drop-in op table for the best-tts hot path on B200.
+
+``BtRuntime.dispatch(op, node_input, node_output, at, env)`` has the signature
+and the semantics of the reference's ``RefRuntime.dispatch``
+(tools/ref_runtime.py:428-668): ``env`` maps tensor names to arrays, an empty
+input name means "absent" (ref_runtime.py:436-439), single-output ops store
+``env[node_output[0]]`` (ref_runtime.py:668), ``Split`` stores each named
+output (ref_runtime.py:536-547) and an op outside the table raises
+``NotImplementedError`` (ref_runtime.py:665-666).
+
+The difference is where the arrays live: values in ``env`` are CUDA tensors
+(torch is used only to own device memory and streams) and every op runs as a
+hand-written sm_100a kernel behind the C ABI of ``libbt_ops.so``.  numpy
+arrays found in ``env`` (constants, initializers) are copied to the device on
+first use and cached; the caller's ``env`` entries are never replaced.
+
+Result dtypes and shapes follow numpy exactly: they are obtained by applying
+the same numpy expression to zero-size arrays of the operands' dtypes, and
+numpy's broadcasting rule.  Errors numpy would raise (bad broadcast, bad
+dtype) surface as the same exceptions before any launch; a status from the
+library raises ``BtError`` (a RuntimeError).
+"""
+import weakref
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import OP, check, load, make_tensor
+
+ONNX_TO_NUMPY = {
+    1: np.float32, 2: np.uint8, 3: np.int8, 4: np.uint16, 5: np.int16,
+    6: np.int32, 7: np.int64, 9: np.bool_, 10: np.float16, 11: np.float64,
+    12: np.uint32, 13: np.uint64,
+}
+
+TORCH_TO_NP = {
+    torch.bool: np.bool_, torch.int8: np.int8, torch.uint8: np.uint8, torch.int16: np.int16,
+    torch.int32: np.int32, torch.int64: np.int64, torch.float16: np.float16,
+    torch.float32: np.float32, torch.float64: np.float64,
+}
+NP_TO_TORCH = {np.dtype(v): k for k, v in TORCH_TO_NP.items()}
+for _name in ("uint16", "uint32", "uint64"):
+    if hasattr(torch, _name):
+        TORCH_TO_NP[getattr(torch, _name)] = getattr(np, _name)
+        NP_TO_TORCH[np.dtype(getattr(np, _name))] = getattr(torch, _name)
+
+UNARY = {"Sqrt": "SQRT", "Exp": "EXP", "Sin": "SIN", "Cos": "COS", "Atan": "ATAN",
+         "Tanh": "TANH", "Sigmoid": "SIGMOID", "Floor": "FLOOR", "Round": "ROUND", "Erf": "ERF"}
+# numpy expressions of the reference (ref_runtime.py:458-489) used only on
+# zero-size arrays, to learn numpy's result dtype.
+_UNARY_NP = {"Sqrt": np.sqrt, "Exp": np.exp, "Sin": np.sin, "Cos": np.cos, "Atan": np.arctan,
+             "Tanh": np.tanh, "Sigmoid": lambda v: 1.0 / (1.0 + np.exp(-v)), "Floor": np.floor,
+             "Round": np.rint, "Erf": None}
+COMPARE = {"Greater": "GREATER", "Less": "LESS", "GreaterOrEqual": "GEQ"}
+
+
+def np_dtype(t):
+    return np.dtype(TORCH_TO_NP[t.dtype])
+
+
+def _wide(dt):
+    """fp16 is widened to fp32 before compute (ref_runtime.py:49-51)."""
+    return np.dtype(np.float32) if dt == np.float16 else np.dtype(dt)
+
+
+def _probe(dt):
+    return np.empty((0,), dtype=dt)
+
+
+def tensor_desc(t):
+    """BtTensor view of a CUDA tensor (element strides, arbitrary layout)."""
+    return make_tensor(t.data_ptr(), np_dtype(t), tuple(t.shape), tuple(t.stride()))
+
+
+class BtRuntime:
+    """Op-table interpreter whose arithmetic runs on the GPU (see module doc)."""
+
+    HOT_OPS = ("Add", "Sub", "Mul", "Div", "Pow", "Sqrt", "Exp", "Sin", "Cos", "Atan", "Tanh",
+               "Sigmoid", "Floor", "Round", "Erf", "LeakyRelu", "Clip", "Equal", "Greater", "Less",
+               "GreaterOrEqual", "And", "Where", "Cast", "ReduceMean", "ReduceSum", "Softmax",
+               "LayerNormalization", "SkipLayerNormalization", "FastGelu", "DequantizeLinear",
+               "Split", "Reshape", "Unsqueeze", "Squeeze")
+
+    def __init__(self, device=None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("BtRuntime needs a CUDA device (there is no CPU fallback)")
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.lib = load()
+        with torch.cuda.device(self.device):
+            check(self.lib.bt_init(self.device.index), "bt_init")
+        self._consts = {}
+        self.launches = 0
+
+    # ---- device values ---------------------------------------------------------
+    def to_device(self, v):
+        """CUDA tensor for an env value (numpy arrays are uploaded once and cached)."""
+        if isinstance(v, torch.Tensor):
+            if not v.is_cuda:
+                v = v.to(self.device)
+            return v
+        a = np.asarray(v)
+        key = id(v)
+        hit = self._consts.get(key)
+        if hit is not None and hit[0]() is v:
+            return hit[1]
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+        try:
+            self._consts[key] = (weakref.ref(v), t)
+        except TypeError:
+            pass
+        return t
+
+    def _empty(self, shape, dt):
+        return torch.empty(tuple(int(s) for s in shape), dtype=NP_TO_TORCH[np.dtype(dt)], device=self.device)
+
+    def _stream(self):
+        check(self.lib.bt_set_stream(ctypes_stream(torch.cuda.current_stream(self.device))), "bt_set_stream")
+
+    # ---- kernels ------------------------------------------------------------------
+    def elementwise(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
+        out = self._empty(out_shape, out_dt)
+        if out.numel() == 0:
+            return out
+        descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
+        attrs = _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(compute_dt)], float(np.float32(alpha)))
+        od = tensor_desc(out)
+        self._stream()
+        check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
+        self.launches += 1
+        return out
+
+    def _widen(self, t):
+        """fp16 tensor -> fp32 copy (kernel), other dtypes unchanged."""
+        if t.dtype == torch.float16:
+            return self.elementwise("IDENTITY", [t], t.shape, np.float32, np.float64)
+        return t
+
+    def _contig(self, t):
+        if t.is_contiguous():
+            return t
+        dt = np_dtype(t)
+        cdt = np.float64 if dt.kind == "f" else np.int64
+        return self.elementwise("IDENTITY", [t], t.shape, dt, cdt)
+
+    # ---- the op table -----------------------------------------------------------------
+    def dispatch(self, op, node_input, node_output, at, env):
+        def arg(i, default=None):
+            if i >= len(node_input) or not node_input[i]:
+                return default
+            return env[node_input[i]]
+
+        def dev(i):
+            v = arg(i)
+            return None if v is None else self.to_device(v)
+
+        if op in ("Add", "Sub", "Mul", "Div", "Pow"):
+            x, y = dev(0), dev(1)
+            a, b = _wide(np_dtype(x)), _wide(np_dtype(y))
+            shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
+            if op == "Div" and a.kind in "iu" and b.kind in "iu":
+                dt = np.floor_divide(_probe(a), _probe(b)).dtype   # ref :452-455
+            else:
+                f = {"Add": np.add, "Sub": np.subtract, "Mul": np.multiply, "Div": np.true_divide,
+                     "Pow": np.power}[op]
+                dt = f(_probe(a), _probe(b)).dtype
+            if op == "Pow" and dt.kind != "f":
+                raise NotImplementedError("integer Pow is not on the GPU path")
+            name = {"Add": "ADD", "Sub": "SUB", "Mul": "MUL", "Div": "DIV", "Pow": "POW"}[op]
+            out = self.elementwise(name, [x, y], shape, dt, self._compute(dt))
+        elif op in UNARY:
+            x = dev(0)
+            a = _wide(np_dtype(x))
+            if op == "Erf":
+                dt = np.dtype(np.float32) if a == np.float32 else np.dtype(np.float64)
+                if a.kind not in "fiub":
+                    raise TypeError(f"Erf of {a}")
+            else:
+                dt = _UNARY_NP[op](_probe(a)).dtype
+            out = self.elementwise(UNARY[op], [x], x.shape, dt, self._compute(dt))
+        elif op == "LeakyRelu":
+            x = dev(0)
+            a = _wide(np_dtype(x))
+            v = _probe(a)
+            dt = np.where(v < 0, v * np.float32(at.get("alpha", 0.01)), v).dtype   # ref :476-479
+            out = self.elementwise("LEAKYRELU", [x], x.shape, dt, self._compute(dt),
+                                   alpha=np.float32(at.get("alpha", 0.01)))
+        elif op == "Clip":
+            x, lo, hi = dev(0), dev(1), dev(2)
+            v = _probe(_wide(np_dtype(x)))
+            if lo is not None:
+                v = np.maximum(v, _probe(_wide(np_dtype(lo))))
+            if hi is not None:
+                v = np.minimum(v, _probe(_wide(np_dtype(hi))))
+            dt = v.dtype
+            if lo is None and hi is None:
+                out = self.elementwise("IDENTITY", [x], x.shape, dt, self._cast_compute(np_dtype(x), dt))
+            else:
+                lo = lo if lo is not None else self._bound(dt, low=True)
+                hi = hi if hi is not None else self._bound(dt, low=False)
+                shape = np.broadcast_shapes(tuple(x.shape), tuple(lo.shape), tuple(hi.shape))
+                out = self.elementwise("CLIP", [x, lo, hi], shape, dt, self._compute(dt))
+        elif op == "Equal":
+            x, y = dev(0), dev(1)
+            ct = np.result_type(np_dtype(x), np_dtype(y))
+            shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
+            out = self.elementwise("EQUAL", [x, y], shape, np.bool_, self._compute(_wide(ct)))
+        elif op in COMPARE:
+            x, y = dev(0), dev(1)
+            ct = np.result_type(_wide(np_dtype(x)), _wide(np_dtype(y)))
+            shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
+            out = self.elementwise(COMPARE[op], [x, y], shape, np.bool_, self._compute(ct))
+        elif op == "And":
+            x, y = dev(0), dev(1)
+            shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
+            out = self.elementwise("AND", [x, y], shape, np.bool_, np.float64)
+        elif op == "Where":
+            c, x, y = dev(0), dev(1), dev(2)
+            dt = np.where(_probe(np.bool_), _probe(np_dtype(x)), _probe(np_dtype(y))).dtype
+            shape = np.broadcast_shapes(tuple(c.shape), tuple(x.shape), tuple(y.shape))
+            out = self.elementwise("WHERE", [c, x, y], shape, dt, self._cast_compute_where(dt))
+        elif op == "Cast":                                      # ref :572-578
+            x = dev(0)
+            target = np.dtype(ONNX_TO_NUMPY[at["to"]])
+            if target == np.float16:
+                target = np.dtype(np.float32)
+            src = _wide(np_dtype(x))
+            out = self.elementwise("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
+        elif op == "DequantizeLinear":                          # ref :631-636
+            q, scale, zp = dev(0), dev(1), dev(2)
+            ins = [q, scale] + ([zp] if zp is not None else [])
+            shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
+            out = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
+        elif op == "FastGelu":                                  # ref :610-611
+            x, b = dev(0), dev(1)
+            x = self._as_f32(x)
+            ins = [x] + ([self._as_f32(b)] if b is not None else [])
+            shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
+            out = self.elementwise("GELU", ins, shape, np.float32, np.float32)
+        elif op in ("ReduceMean", "ReduceSum"):                 # ref :589-598
+            axes = arg(1) if len(node_input) > 1 else at.get("axes")
+            out = self._reduce(op, dev(0), axes, at)
+        elif op == "Softmax":                                   # ref :599-600
+            x = self._as_f32(dev(0))
+            out = self.softmax(x, None, int(at.get("axis", -1)))
+        elif op == "LayerNormalization":                        # ref :601-603
+            out = self.layernorm(dev(0), None, None, dev(1), dev(2), int(at.get("axis", -1)),
+                                 at.get("epsilon", 1e-5))
+        elif op == "SkipLayerNormalization":                    # ref :604-609
+            out = self.layernorm(dev(0), dev(1), dev(4), dev(2), dev(3), -1, at.get("epsilon", 1e-12))
+        elif op == "Split":                                     # ref :536-547 (views)
+            x = dev(0)
+            axis = int(at.get("axis", 0)) % max(1, x.dim())
+            sizes = arg(1)
+            if sizes is None:
+                parts = np.array_split(np.empty(x.shape[axis], np.int8), len(node_output))
+                sizes = [len(p) for p in parts]
+            else:
+                sizes = [int(s) for s in np.asarray(sizes if not isinstance(sizes, torch.Tensor)
+                                                    else sizes.cpu().numpy()).reshape(-1)]
+            for name, p in zip(node_output, torch.split(x, sizes, dim=axis)):
+                if name:
+                    env[name] = p
+            return
+        elif op == "Reshape":                                   # ref :511-516 (view)
+            x = dev(0)
+            shape = [int(s) for s in _host_ints(arg(1))]
+            if not at.get("allowzero", 0):
+                shape = [x.shape[i] if s == 0 else s for i, s in enumerate(shape)]
+            out = x.reshape(shape)
+        elif op == "Unsqueeze":                                 # ref :519-523 (view)
+            x = dev(0)
+            axes = arg(1) if len(node_input) > 1 else at.get("axes")
+            out = x
+            for a in sorted(int(v) for v in _host_ints(axes)):
+                out = out.unsqueeze(a)
+        elif op == "Squeeze":                                   # ref :524-530 (view)
+            x = dev(0)
+            axes = arg(1) if len(node_input) > 1 else at.get("axes")
+            if axes is None:
+                out = x.reshape([s for s in x.shape if s != 1])
+            else:
+                out = x
+                for a in sorted((int(v) % x.dim() for v in _host_ints(axes)), reverse=True):
+                    if out.shape[a] != 1:
+                        raise ValueError("cannot select an axis to squeeze out which has size not equal to one")
+                    out = out.squeeze(a)
+        else:
+            raise NotImplementedError(f"{op} ({node_output}) is not on the B200 path")
+        env[node_output[0]] = out
+
+    def run_nodes(self, nodes, env):
+        """Executes ``(op, inputs, outputs, attrs)`` nodes in order, wrapping
+        failures like the reference's drivers (ref_runtime.py:398-403)."""
+        for op, ins, outs, at in nodes:
+            try:
+                self.dispatch(op, list(ins), list(outs), dict(at or {}), env)
+            except Exception as exc:
+                raise RuntimeError(f"{op} {list(outs)} failed: {exc}") from exc
+        return env
+
+    # ---- helpers --------------------------------------------------------------------------
+    @staticmethod
+    def _compute(dt):
+        dt = np.dtype(dt)
+        if dt == np.float16:
+            return np.dtype(np.float32)
+        if dt.kind == "f":
+            return dt
+        if dt.kind == "b":
+            return np.dtype(np.int64)
+        return np.dtype(np.uint64) if dt == np.uint64 else np.dtype(np.int64)
+
+    @staticmethod
+    def _cast_compute(src, dst):
+        src, dst = np.dtype(src), np.dtype(dst)
+        if src.kind in "iub" and dst.kind in "iub":
+            return np.dtype(np.int64)
+        if src.kind in "iub" and dst.kind == "f":
+            return np.dtype(np.int64)
+        return np.dtype(np.float64)
+
+    def _cast_compute_where(self, dt):
+        return np.dtype(np.float64) if np.dtype(dt).kind == "f" else np.dtype(np.int64)
+
+    def _bound(self, dt, low):
+        dt = np.dtype(dt)
+        if dt.kind == "f":
+            v = -np.inf if low else np.inf
+        elif dt.kind == "b":
+            v = False if low else True
+        else:
+            info = np.iinfo(dt)
+            v = info.min if low else info.max
+        return torch.tensor(np.array(v, dtype=dt)).to(self.device)
+
+    def _as_f32(self, t):
+        dt = np_dtype(t)
+        if dt == np.float32:
+            return t
+        return self.elementwise("IDENTITY", [t], t.shape, np.float32, self._cast_compute(dt, np.float32))
+
+    def _reduce(self, op, x, axes_in, at):
+        x = self._widen(x)
+        keep = bool(at.get("keepdims", 1))
+        if axes_in is None:
+            if at.get("noop_with_empty_axes", 0):
+                return x
+            axes = tuple(range(x.dim()))
+        else:
+            axes = tuple(int(a) for a in _host_ints(axes_in))
+            if len(axes) == 0:
+                return x
+        nd = x.dim()
+        for a in axes:
+            if not -nd <= a < nd:
+                raise np.exceptions.AxisError(a, nd)
+        norm = sorted(set(a % nd for a in axes))
+        if len(norm) != len(axes):
+            raise ValueError("duplicate value in 'axis'")
+        dt = np_dtype(x)
+        if dt != np.float32:
+            raise NotImplementedError(f"{op} of {dt} is not on the GPU path (float32/float16 only)")
+        x = self._contig(x)
+        kind = 1 if op == "ReduceMean" else 0
+        out_shape = [1 if i in norm else s for i, s in enumerate(x.shape)] if keep else \
+            [s for i, s in enumerate(x.shape) if i not in norm]
+        if x.numel() == 0 or any(x.shape[i] == 0 for i in norm):
+            fill = 0.0 if kind == 0 else float("nan")
+            return torch.full(out_shape, fill, dtype=torch.float32, device=self.device)
+        # numpy reduces one contiguous block of axes in a single pass:
+        # pairwise over the block when it is innermost, slice after slice
+        # (lexicographic order) otherwise.  Two blocks whose inner block is
+        # innermost are the pairwise row sums added slice after slice over
+        # the outer block, which is two passes here.  Other axis sets would
+        # interleave the outer chains differently and are not on the GPU path.
+        blocks = _axis_blocks(norm, x.shape)
+        if len(blocks) == 1:
+            return self._reduce_block(x, blocks[0], kind).reshape(out_shape)
+        innermost = all(s == 1 for s in x.shape[blocks[1][-1] + 1:])
+        if len(blocks) == 2 and innermost:
+            rows = self._reduce_block(x, blocks[1], 0)
+            total = self._reduce_block(rows, blocks[0], 0)
+            if kind == 1:
+                count = int(np.prod([x.shape[i] for i in norm]))
+                total = self._mean_from_sum(total, count)
+            return total.reshape(out_shape)
+        raise NotImplementedError(f"{op} over axes {axes} of shape {tuple(x.shape)} is not on the GPU path")
+
+    def _reduce_block(self, x, blk, kind):
+        """Reduces the contiguous axis block ``blk`` of x with keepdims=1."""
+        n_axes = len(blk)
+        axes = (ctypes_i64 * n_axes)(*blk)
+        out_shape = [1 if i in blk else s for i, s in enumerate(x.shape)]
+        out = self._empty(out_shape, np.float32)
+        self._stream()
+        check(self.lib.bt_reduce(kind, tensor_desc(x), axes, n_axes, 1, tensor_desc(out)), "bt_reduce")
+        self.launches += 1
+        return out
+
+    def _mean_from_sum(self, s, count):
+        # np.mean divides the float32 sum by an intp count: float64 division,
+        # rounded to float32.
+        c = torch.tensor(np.array(count, dtype=np.int64)).to(self.device)
+        return self.elementwise("DIV", [s, c], s.shape, np.float32, np.float64)
+
+    def softmax(self, x, mask, axis):
+        x = self._contig(x)
+        out = self._empty(x.shape, np.float32)
+        if out.numel() == 0:
+            return out
+        nd = x.dim()
+        if axis < -nd or axis >= max(nd, 1):
+            raise np.exceptions.AxisError(axis, nd)
+        self._stream()
+        check(self.lib.bt_softmax(tensor_desc(x), tensor_desc(mask) if mask is not None else None, axis,
+                                  tensor_desc(out)), "bt_softmax")
+        self.launches += 1
+        return out
+
+    def layernorm(self, x, skip, bias, gamma, beta, axis, eps):
+        x = self._contig(self._as_f32(x))
+        if skip is not None:
+            skip = self._contig(self._as_f32(skip))
+            if tuple(skip.shape) != tuple(x.shape):
+                raise NotImplementedError("SkipLayerNormalization with a broadcast skip is not on the GPU path")
+        if bias is not None:
+            bias = self._contig(self._as_f32(bias))
+        nd = x.dim()
+        ax = axis % nd
+        trailing = tuple(x.shape[ax:])
+        gamma = self._fit_param(gamma, trailing)
+        beta = self._fit_param(beta, trailing) if beta is not None else None
+        if bias is not None:
+            bias = self._fit_param(bias, trailing)
+        out = self._empty(x.shape, np.float32)
+        if out.numel() == 0:
+            return out
+        self._stream()
+        check(self.lib.bt_layernorm(tensor_desc(x), tensor_desc(skip) if skip is not None else None,
+                                    tensor_desc(bias) if bias is not None else None, tensor_desc(gamma),
+                                    tensor_desc(beta) if beta is not None else None, axis,
+                                    float(np.float32(eps)), tensor_desc(out)), "bt_layernorm")
+        self.launches += 1
+        return out
+
+    # ---- fused entry points (beyond the one-op-per-node table) ---------------------
+    def chain(self, prog, inputs, out_shape):
+        """Runs a bt_chain register program (float32) over broadcast inputs."""
+        out = self._empty(out_shape, np.float32)
+        if out.numel() == 0:
+            return out
+        descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
+        self._stream()
+        check(self.lib.bt_fused_chain(ctypes.byref(prog), descs, tensor_desc(out)), "bt_fused_chain")
+        self.launches += 1
+        return out
+
+    def dequant_mul(self, q, scale, zero_point, gain):
+        """Mul(DequantizeLinear(q, scale, zero_point), gain) in one pass: the
+        c4 weight path, rounded like the two reference ops
+        (ref_runtime.py:631-636 then :450-451)."""
+        ins = [q, scale, gain] + ([zero_point] if zero_point is not None else [])
+        prog = _lib.BtChain()
+        prog.n_in = len(ins)
+        code = []
+        src = 0
+        if zero_point is not None:
+            code.append((OP["SUB"], 4, 0, 3))    # r4 = q - zp
+            src = 4
+        code.append((OP["MUL"], 4, src, 1))      # r4 = (q - zp) * scale
+        code.append((OP["MUL"], 4, 4, 2))        # r4 = r4 * gain
+        for i, (op, d, a, b) in enumerate(code):
+            prog.instr[i] = _lib.BtChainInstr(op, d, a, b, 0.0)
+        prog.n_instr = len(code)
+        prog.out_reg = 4
+        shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
+        return self.chain(prog, ins, shape)
+
+    def adain_snake(self, srcs, gain, shift, eps, alpha=None, inv_alpha=None, res=None, outs=None):
+        """Row-fused AdaIN1d (+ Snake) of [B, C, T] float32 tensors (see
+        bt_adain_snake in bt_ops.h).  gain / shift are [B, C] float32 views
+        with unit channel stride; alpha / inv_alpha [C] (fp16 or fp32)."""
+        x0 = srcs[0]
+        B, Cc, T = x0.shape
+        a = _lib.BtAdainArgs()
+        a.rows, a.cols, a.channels = B * Cc, T, Cc
+        a.n_src = len(srcs)
+        for i, s in enumerate(srcs):
+            assert s.is_contiguous() and s.dtype == torch.float32 and tuple(s.shape) == (B, Cc, T)
+            a.src[i] = s.data_ptr()
+        a.res = res.data_ptr() if res is not None else None
+        a.eps = float(np.float32(eps))
+        gains = gain if isinstance(gain, (list, tuple)) else [gain]
+        shifts = shift if isinstance(shift, (list, tuple)) else [shift]
+        alphas = alpha if isinstance(alpha, (list, tuple)) else [alpha] * len(gains)
+        invs = inv_alpha if isinstance(inv_alpha, (list, tuple)) else [inv_alpha] * len(gains)
+        a.n_out = len(gains)
+        a.gain_stride = gains[0].stride(0)
+        a.shift_stride = shifts[0].stride(0)
+        a.alpha_dtype = _lib.BT_F16
+        if outs is None:
+            outs = [self._empty((B, Cc, T), np.float32) for _ in gains]
+        for i in range(len(gains)):
+            assert gains[i].stride(-1) == 1 and shifts[i].stride(-1) == 1
+            assert gains[i].stride(0) == a.gain_stride and shifts[i].stride(0) == a.shift_stride
+            a.gain[i] = gains[i].data_ptr()
+            a.shift[i] = shifts[i].data_ptr()
+            if alphas[i] is not None:
+                a.alpha_dtype = _lib.NP_TO_BT[np_dtype(alphas[i])]
+                a.alpha[i] = alphas[i].data_ptr()
+                a.inv_alpha[i] = invs[i].data_ptr()
+            a.out[i] = outs[i].data_ptr()
+        self._stream()
+        check(self.lib.bt_adain_snake(ctypes.byref(a)), "bt_adain_snake")
+        self.launches += 1
+        return outs
+
+    def _fit_param(self, p, trailing):
+        """gamma/beta as a contiguous run over the normalised axes (broadcast
+        materialised by a kernel when needed)."""
+        if tuple(p.shape) == trailing and p.is_contiguous():
+            return p
+        shape = np.broadcast_shapes(tuple(p.shape), trailing)
+        if shape != trailing:
+            raise ValueError(f"parameter of shape {tuple(p.shape)} does not broadcast to {trailing}")
+        dt = np_dtype(p)
+        return self.elementwise("IDENTITY", [p], trailing, dt if dt.kind == "f" else np.float32,
+                                np.float64)
+
+
+def _axis_blocks(axes, shape):
+    """Groups sorted axes into runs that are contiguous once size-1 axes are ignored."""
+    blocks = []
+    for a in axes:
+        if blocks:
+            prev = blocks[-1][-1]
+            if all(shape[i] == 1 for i in range(prev + 1, a)):
+                blocks[-1].append(a)
+                continue
+        blocks.append([a])
+    return blocks
+
+
+def _host_ints(v):
+    if v is None:
+        return []
+    if isinstance(v, torch.Tensor):
+        v = v.detach().cpu().numpy()
+    return np.asarray(v).reshape(-1).tolist()
+
+
+def ctypes_stream(stream):
+    return stream.cuda_stream
+
+
+import ctypes  # noqa: E402
+
+ctypes_i64 = ctypes.c_int64

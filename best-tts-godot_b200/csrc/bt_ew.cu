@@ -1,0 +1,627 @@
+// bt_ew.cu -- broadcast elementwise engine for sm_100a.
+//
+// One call = one numpy ufunc application (tools/ref_runtime.py:446-503,
+// :572-578, :610-611, :631-636).  The host planner (bt_host.cpp) broadcasts
+// every operand view to the output shape and merges contiguous axes; the
+// launcher then picks one of three kernels:
+//   flat  -- one axis, every operand contiguous (stride 1) or a scalar
+//            (stride 0): 4-element vector loads/stores (128-bit for fp32),
+//            grid-stride over SM-count-multiple grids;
+//   rows  -- two axes [R, T] with unit or zero inner strides (per-row scale,
+//            per-column bias, full tensors): vectorised along T when every
+//            row start is 16-byte aligned;
+//   nd    -- any rank up to 8, coordinates unravelled per element.
+// Every path rounds each op once in its compute type (no contraction; the
+// float32 transcendentals are numpy's own algorithms, see bt_core.h).
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include "bt_ops.h"
+#include "bt_internal.h"
+#include "bt_core.h"
+
+namespace bt {
+namespace {
+
+struct Operand {
+  const void* p;
+  int32_t dt;
+  int32_t pad;
+  int64_t st[BT_MAX_RANK];
+};
+
+struct EwArgs {
+  int32_t op, n_in, rank, cdt;
+  float alpha;
+  int32_t odt;
+  int64_t n;
+  int64_t shape[BT_MAX_RANK];
+  Operand in[3];
+  void* out;
+  int64_t ost[BT_MAX_RANK];
+};
+
+// ---- element load / store with numpy conversion semantics ----------------
+template <class CT>
+__device__ __forceinline__ CT ld1(const void* p, int dt, int64_t i) {
+  switch (dt) {
+    case BT_F32: return (CT)__ldg((const float*)p + i);
+    case BT_F16: return (CT)__half2float(__ldg((const __half*)p + i));
+    case BT_F64: return (CT)__ldg((const double*)p + i);
+    case BT_I8: return (CT)(signed char)__ldg((const char*)p + i);
+    case BT_U8: return (CT)__ldg((const unsigned char*)p + i);
+    case BT_BOOL: return (CT)(__ldg((const unsigned char*)p + i) != 0);
+    case BT_I16: return (CT)__ldg((const short*)p + i);
+    case BT_U16: return (CT)__ldg((const unsigned short*)p + i);
+    case BT_I32: return (CT)__ldg((const int*)p + i);
+    case BT_U32: return (CT)__ldg((const unsigned int*)p + i);
+    case BT_I64: return (CT)__ldg((const long long*)p + i);
+    case BT_U64: return (CT)__ldg((const unsigned long long*)p + i);
+  }
+  return CT(0);
+}
+
+// Float to integer conversion as numpy's C casts compile on x86-64:
+// truncation toward zero through a 32-bit (or, for uint32 / int64 / uint64,
+// a 64-bit) cvtt, whose out-of-range and NaN result is the "integer
+// indefinite" INT_MIN; narrower targets keep the low bits.
+__device__ __forceinline__ int32_t cvtt32(double v) {
+  if (!(v > -2147483649.0 && v < 2147483648.0)) return INT32_MIN;
+  return (int32_t)v;
+}
+__device__ __forceinline__ int64_t cvtt64(double v) {
+  if (!(v > -9223372036854775808.0 && v < 9223372036854775808.0)) return INT64_MIN;
+  return (int64_t)v;
+}
+__device__ __forceinline__ uint64_t cvtt_u64(double v) {
+  if (v < 9223372036854775808.0) return (uint64_t)cvtt64(v);
+  return (uint64_t)cvtt64(v - 9223372036854775808.0) ^ 0x8000000000000000ull;
+}
+
+template <class CT>
+__device__ __forceinline__ void st1(void* p, int dt, int64_t i, CT v) {
+  constexpr bool kFloat = (CT(0.5) != CT(0));
+  switch (dt) {
+    case BT_F32: ((float*)p)[i] = (float)v; return;
+    case BT_F64: ((double*)p)[i] = (double)v; return;
+    case BT_F16: ((__half*)p)[i] = __double2half((double)v); return;
+    case BT_BOOL: ((unsigned char*)p)[i] = (v != CT(0)) ? 1 : 0; return;
+    default: break;
+  }
+  if (kFloat) {
+    double d = (double)v;
+    switch (dt) {
+      case BT_I8: ((int8_t*)p)[i] = (int8_t)cvtt32(d); return;
+      case BT_U8: ((uint8_t*)p)[i] = (uint8_t)cvtt32(d); return;
+      case BT_I16: ((int16_t*)p)[i] = (int16_t)cvtt32(d); return;
+      case BT_U16: ((uint16_t*)p)[i] = (uint16_t)cvtt32(d); return;
+      case BT_I32: ((int32_t*)p)[i] = cvtt32(d); return;
+      case BT_U32: ((uint32_t*)p)[i] = (uint32_t)cvtt64(d); return;
+      case BT_I64: ((int64_t*)p)[i] = cvtt64(d); return;
+      case BT_U64: ((uint64_t*)p)[i] = cvtt_u64(d); return;
+    }
+  } else {
+    long long w = (long long)v;
+    switch (dt) {
+      case BT_I8: ((int8_t*)p)[i] = (int8_t)w; return;
+      case BT_U8: ((uint8_t*)p)[i] = (uint8_t)w; return;
+      case BT_I16: ((int16_t*)p)[i] = (int16_t)w; return;
+      case BT_U16: ((uint16_t*)p)[i] = (uint16_t)w; return;
+      case BT_I32: ((int32_t*)p)[i] = (int32_t)w; return;
+      case BT_U32: ((uint32_t*)p)[i] = (uint32_t)w; return;
+      case BT_I64: ((int64_t*)p)[i] = (int64_t)w; return;
+      case BT_U64: ((uint64_t*)p)[i] = (uint64_t)w; return;
+    }
+  }
+}
+
+// ---- numpy op semantics per compute type ----------------------------------
+// np.maximum / np.minimum: NaN propagates; for equal operands (including
+// +0 / -0) the second operand is returned.
+template <class T>
+__device__ __forceinline__ T np_max(T a, T b) { return (a != a) ? a : ((b != b) ? b : (a > b ? a : b)); }
+template <class T>
+__device__ __forceinline__ T np_min(T a, T b) { return (a != a) ? a : ((b != b) ? b : (a < b ? a : b)); }
+
+__device__ __forceinline__ float np_powf(float a, float b) {
+  if (b == 2.0f) return BT_MUL(a, a);   // numpy's power for exponent 2 is x*x
+  return (float)pow((double)a, (double)b);
+}
+
+// tanh form of GELU in the reference's evaluation order
+// 0.5*x*(1.0 + tanh(k*(x + 0.044715*x*x*x))) (ref_runtime.py:288-293).
+__device__ __forceinline__ float np_fast_gelu(float x) {
+  const float k = 0.7978845608028654f;
+  float a = BT_MUL(0.5f, x);
+  float c = BT_MUL(BT_MUL(BT_MUL(0.044715f, x), x), x);
+  float f = BT_MUL(k, BT_ADD(x, c));
+  float g = (float)tanh((double)f);
+  return BT_MUL(a, BT_ADD(1.0f, g));
+}
+
+__device__ __forceinline__ float apply_f32(int op, float a, float b, float c, float alpha, int n_in) {
+  switch (op) {
+    case BT_OP_ADD: return BT_ADD(a, b);
+    case BT_OP_SUB: return BT_SUB(a, b);
+    case BT_OP_MUL: return BT_MUL(a, b);
+    case BT_OP_DIV: return BT_DIV(a, b);
+    case BT_OP_POW: return np_powf(a, b);
+    case BT_OP_SQRT: return BT_SQRT(a);
+    case BT_OP_EXP: return np_expf(a);
+    case BT_OP_SIN: return np_sinf(a);
+    case BT_OP_COS: return np_cosf(a);
+    case BT_OP_ATAN: return (float)atan((double)a);
+    case BT_OP_TANH: return (float)tanh((double)a);
+    case BT_OP_SIGMOID: return np_sigmoidf(a);
+    case BT_OP_FLOOR: return floorf(a);
+    case BT_OP_ROUND: return rintf(a);
+    case BT_OP_LEAKYRELU: return a < 0.0f ? BT_MUL(a, alpha) : a;
+    case BT_OP_CLIP: return np_min(np_max(a, b), c);
+    case BT_OP_EQUAL: return a == b ? 1.0f : 0.0f;
+    case BT_OP_GREATER: return a > b ? 1.0f : 0.0f;
+    case BT_OP_LESS: return a < b ? 1.0f : 0.0f;
+    case BT_OP_GEQ: return a >= b ? 1.0f : 0.0f;
+    case BT_OP_NEG: return -a;
+    case BT_OP_ABS: return fabsf(a);
+    case BT_OP_LOG: return (float)log((double)a);
+    case BT_OP_MIN: return np_min(a, b);
+    case BT_OP_MAX: return np_max(a, b);
+    case BT_OP_ERF: return (float)erf((double)a);
+    case BT_OP_GELU: return np_fast_gelu(n_in > 1 ? BT_ADD(a, b) : a);
+    case BT_OP_DEQUANT: return BT_MUL(n_in > 2 ? BT_SUB(a, c) : a, b);
+    default: return a;  // CAST_INT / CAST_BOOL / IDENTITY: conversion only
+  }
+}
+
+__device__ __forceinline__ double apply_f64(int op, double a, double b, double c, float alpha, int n_in) {
+  switch (op) {
+    case BT_OP_ADD: return __dadd_rn(a, b);
+    case BT_OP_SUB: return __dsub_rn(a, b);
+    case BT_OP_MUL: return __dmul_rn(a, b);
+    case BT_OP_DIV: return __ddiv_rn(a, b);
+    case BT_OP_POW: return b == 2.0 ? __dmul_rn(a, a) : pow(a, b);
+    case BT_OP_SQRT: return __dsqrt_rn(a);
+    case BT_OP_EXP: return exp(a);
+    case BT_OP_SIN: return sin(a);
+    case BT_OP_COS: return cos(a);
+    case BT_OP_ATAN: return atan(a);
+    case BT_OP_TANH: return tanh(a);
+    case BT_OP_SIGMOID: return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-a)));
+    case BT_OP_FLOOR: return floor(a);
+    case BT_OP_ROUND: return rint(a);
+    case BT_OP_LEAKYRELU: return a < 0.0 ? __dmul_rn(a, (double)alpha) : a;
+    case BT_OP_CLIP: return np_min(np_max(a, b), c);
+    case BT_OP_EQUAL: return a == b ? 1.0 : 0.0;
+    case BT_OP_GREATER: return a > b ? 1.0 : 0.0;
+    case BT_OP_LESS: return a < b ? 1.0 : 0.0;
+    case BT_OP_GEQ: return a >= b ? 1.0 : 0.0;
+    case BT_OP_NEG: return -a;
+    case BT_OP_ABS: return fabs(a);
+    case BT_OP_LOG: return log(a);
+    case BT_OP_MIN: return np_min(a, b);
+    case BT_OP_MAX: return np_max(a, b);
+    case BT_OP_ERF: return erf(a);
+    default: return a;
+  }
+}
+
+__device__ __forceinline__ long long floor_div_i64(long long a, long long b) {
+  if (b == 0) return 0;                               // numpy: 0 (and a warning)
+  if (a == INT64_MIN && b == -1) return INT64_MIN;    // numpy: overflow -> MIN
+  long long q = a / b;
+  if ((a % b != 0) && ((a < 0) != (b < 0))) q -= 1;
+  return q;
+}
+
+__device__ __forceinline__ long long apply_i64(int op, long long a, long long b, long long c, float, int) {
+  switch (op) {
+    case BT_OP_ADD: return (long long)((unsigned long long)a + (unsigned long long)b);
+    case BT_OP_SUB: return (long long)((unsigned long long)a - (unsigned long long)b);
+    case BT_OP_MUL: return (long long)((unsigned long long)a * (unsigned long long)b);
+    case BT_OP_DIV: return floor_div_i64(a, b);
+    case BT_OP_CLIP: return a < b ? b : (a > c ? c : a);
+    case BT_OP_EQUAL: return a == b;
+    case BT_OP_GREATER: return a > b;
+    case BT_OP_LESS: return a < b;
+    case BT_OP_GEQ: return a >= b;
+    case BT_OP_NEG: return (long long)(0ull - (unsigned long long)a);
+    case BT_OP_ABS: return a < 0 ? (long long)(0ull - (unsigned long long)a) : a;
+    case BT_OP_MIN: return a < b ? a : b;
+    case BT_OP_MAX: return a > b ? a : b;
+    default: return a;
+  }
+}
+
+template <class CT> struct Apply;
+template <> struct Apply<float> {
+  static __device__ __forceinline__ float f(int op, float a, float b, float c, float al, int n) { return apply_f32(op, a, b, c, al, n); }
+};
+template <> struct Apply<double> {
+  static __device__ __forceinline__ double f(int op, double a, double b, double c, float al, int n) { return apply_f64(op, a, b, c, al, n); }
+};
+template <> struct Apply<long long> {
+  static __device__ __forceinline__ long long f(int op, long long a, long long b, long long c, float al, int n) { return apply_i64(op, a, b, c, al, n); }
+};
+
+// One output element given the operands' element offsets.
+template <class CT>
+__device__ __forceinline__ void ew_element(const EwArgs& a, const int64_t* off, int64_t oo) {
+  if (a.op == BT_OP_WHERE) {
+    bool cond = ld1<double>(a.in[0].p, a.in[0].dt, off[0]) != 0.0;
+    int k = cond ? 1 : 2;
+    st1<CT>(a.out, a.odt, oo, ld1<CT>(a.in[k].p, a.in[k].dt, off[k]));
+    return;
+  }
+  if (a.op == BT_OP_AND) {
+    bool r = ld1<double>(a.in[0].p, a.in[0].dt, off[0]) != 0.0 &&
+             ld1<double>(a.in[1].p, a.in[1].dt, off[1]) != 0.0;
+    st1<CT>(a.out, a.odt, oo, r ? CT(1) : CT(0));
+    return;
+  }
+  CT x = ld1<CT>(a.in[0].p, a.in[0].dt, off[0]);
+  CT y = a.n_in > 1 ? ld1<CT>(a.in[1].p, a.in[1].dt, off[1]) : CT(0);
+  CT z = a.n_in > 2 ? ld1<CT>(a.in[2].p, a.in[2].dt, off[2]) : CT(0);
+  st1<CT>(a.out, a.odt, oo, Apply<CT>::f(a.op, x, y, z, a.alpha, a.n_in));
+}
+
+// ---- kernels ------------------------------------------------------------------
+template <class CT>
+__global__ void __launch_bounds__(256) ew_nd_kernel(EwArgs a) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    int64_t rem = i, off[3] = {0, 0, 0}, oo = 0;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      int64_t ext = a.shape[d];
+      int64_t c = rem % ext;
+      rem /= ext;
+      for (int k = 0; k < 3; ++k) off[k] += c * a.in[k].st[d];
+      oo += c * a.ost[d];
+    }
+    ew_element<CT>(a, off, oo);
+  }
+}
+
+// Flat (rank 1) float32 path: every input is a scalar or a unit-stride run,
+// the output is a unit-stride run.  VEC = 4 when every unit-stride operand
+// starts on a 4-element boundary of its own type.
+template <int VEC>
+__global__ void __launch_bounds__(256) ew_flat_kernel(EwArgs a) {
+  const int64_t nv = a.n / VEC;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+    const int64_t base = v * VEC;
+    float x[3][VEC];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      if (k >= a.n_in) break;
+      const Operand& o = a.in[k];
+      if (o.st[0] == 0) {
+        float s = ld1<float>(o.p, o.dt, 0);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) x[k][j] = s;
+      } else if (VEC == 4 && o.dt == BT_F32) {
+        float4 f = __ldcs((const float4*)((const float*)o.p + base));
+        x[k][0] = f.x; x[k][1] = f.y; x[k][2] = f.z; x[k][3] = f.w;
+      } else if (VEC == 4 && o.dt == BT_F16) {
+        uint2 u = __ldcs((const uint2*)((const __half*)o.p + base));
+        __half2 h0 = *reinterpret_cast<__half2*>(&u.x), h1 = *reinterpret_cast<__half2*>(&u.y);
+        float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        x[k][0] = f0.x; x[k][1] = f0.y; x[k][2] = f1.x; x[k][3] = f1.y;
+      } else if (VEC == 4 && o.dt == BT_I8) {
+        int w = __ldcs((const int*)((const signed char*)o.p + base));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[k][j] = (float)(signed char)(w >> (8 * j));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) x[k][j] = ld1<float>(o.p, o.dt, base + j);
+      }
+    }
+    float r[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j)
+      r[j] = apply_f32(a.op, x[0][j], a.n_in > 1 ? x[1][j] : 0.f, a.n_in > 2 ? x[2][j] : 0.f, a.alpha, a.n_in);
+    if (VEC == 4 && a.odt == BT_F32) {
+      __stcs((float4*)((float*)a.out + base), make_float4(r[0], r[1], r[2], r[3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, base + j, r[j]);
+    }
+  }
+  // tail
+  const int64_t t0 = nv * VEC;
+  const int64_t i = t0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < a.n) {
+    int64_t off[3];
+    for (int k = 0; k < 3; ++k) off[k] = i * a.in[k].st[0];
+    float x0 = ld1<float>(a.in[0].p, a.in[0].dt, off[0]);
+    float x1 = a.n_in > 1 ? ld1<float>(a.in[1].p, a.in[1].dt, off[1]) : 0.f;
+    float x2 = a.n_in > 2 ? ld1<float>(a.in[2].p, a.in[2].dt, off[2]) : 0.f;
+    st1<float>(a.out, a.odt, i, apply_f32(a.op, x0, x1, x2, a.alpha, a.n_in));
+  }
+}
+
+// [R, T] float32 path: operand k's element (r, t) is at r*st0 + t*st1 with
+// st1 in {0, 1}; the output is contiguous.  blockIdx.y walks rows.
+template <int VEC>
+__global__ void __launch_bounds__(256) ew_rows_kernel(EwArgs a) {
+  const int64_t R = a.shape[0], T = a.shape[1];
+  const int64_t nv = T / VEC;
+  for (int64_t r = blockIdx.y; r < R; r += gridDim.y) {
+    float rowv[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      if (k < a.n_in && a.in[k].st[1] == 0) rowv[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0]);
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = v * VEC;
+      float x[3][VEC];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        if (k >= a.n_in) break;
+        const Operand& o = a.in[k];
+        if (o.st[1] == 0) {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) x[k][j] = rowv[k];
+        } else if (VEC == 4 && o.dt == BT_F32) {
+          float4 f = (o.st[0] == 0) ? __ldg((const float4*)((const float*)o.p + t))
+                                    : __ldcs((const float4*)((const float*)o.p + r * o.st[0] + t));
+          x[k][0] = f.x; x[k][1] = f.y; x[k][2] = f.z; x[k][3] = f.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) x[k][j] = ld1<float>(o.p, o.dt, r * o.st[0] + t + j);
+        }
+      }
+      float res[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        res[j] = apply_f32(a.op, x[0][j], a.n_in > 1 ? x[1][j] : 0.f, a.n_in > 2 ? x[2][j] : 0.f, a.alpha, a.n_in);
+      const int64_t ob = r * a.ost[0] + t;
+      if (VEC == 4 && a.odt == BT_F32) {
+        __stcs((float4*)((float*)a.out + ob), make_float4(res[0], res[1], res[2], res[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, ob + j, res[j]);
+      }
+    }
+    // tail of the row
+    for (int64_t t = nv * VEC + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < T;
+         t += (int64_t)gridDim.x * blockDim.x) {
+      float x[3] = {0.f, 0.f, 0.f};
+      for (int k = 0; k < a.n_in; ++k) x[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0] + t * a.in[k].st[1]);
+      st1<float>(a.out, a.odt, r * a.ost[0] + t, apply_f32(a.op, x[0], x[1], x[2], a.alpha, a.n_in));
+    }
+  }
+}
+
+// ---- fused chain (register program) ---------------------------------------------
+struct ChainArgs {
+  bt_chain prog;
+  int32_t rank;
+  int32_t odt;
+  int64_t n;
+  int64_t shape[BT_MAX_RANK];
+  const void* p[BT_CHAIN_MAX_IN];
+  int32_t dt[BT_CHAIN_MAX_IN];
+  int64_t st[BT_CHAIN_MAX_IN][BT_MAX_RANK];
+  void* out;
+  int64_t ost[BT_MAX_RANK];
+};
+
+__device__ __forceinline__ float run_chain(const bt_chain& pg, float* r) {
+#pragma unroll 1
+  for (int k = 0; k < pg.n_instr; ++k) {
+    const bt_chain_instr& ins = pg.instr[k];
+    r[ins.dst] = apply_f32(ins.op, r[ins.a], r[ins.b], 0.0f, ins.alpha, 2);
+  }
+  return r[pg.out_reg];
+}
+
+constexpr int kChainRegs = 16;
+
+__global__ void __launch_bounds__(256) chain_kernel(ChainArgs a) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    int64_t rem = i, off[BT_CHAIN_MAX_IN] = {0, 0, 0, 0, 0, 0}, oo = 0;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      int64_t ext = a.shape[d];
+      int64_t c = rem % ext;
+      rem /= ext;
+      for (int k = 0; k < BT_CHAIN_MAX_IN; ++k) off[k] += c * a.st[k][d];
+      oo += c * a.ost[d];
+    }
+    float r[kChainRegs];
+    for (int k = 0; k < a.prog.n_in; ++k) r[k] = ld1<float>(a.p[k], a.dt[k], off[k]);
+    st1<float>(a.out, a.odt, oo, run_chain(a.prog, r));
+  }
+}
+
+// ---- launch helpers ---------------------------------------------------------------
+int grid_for(int64_t work, int threads) {
+  DevInfo di;
+  int sms = 148;
+  if (dev_info(&di) == BT_OK && di.sm_count > 0) sms = di.sm_count;
+  int64_t blocks = (work + threads - 1) / threads;
+  int64_t cap = (int64_t)sms * 8;  // 8 resident 256-thread CTAs per SM
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (int)blocks;
+}
+
+bool aligned_run(const void* p, int dt, int vec) {
+  return ((uintptr_t)p % (uintptr_t)(dtype_size(dt) * vec)) == 0;
+}
+
+}  // namespace
+}  // namespace bt
+
+using namespace bt;
+
+extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_tensor* out,
+                              const bt_ew_attrs* attrs) {
+  if (n_in < 1 || n_in > 3) return set_error(BT_EINVAL, "bt_elementwise: n_in %d outside 1..3", n_in);
+  if (!in || !out || !attrs) return set_error(BT_EINVAL, "bt_elementwise: null argument");
+  const bool known = (op >= 0 && op <= 31) || op == BT_OP_DEQUANT;
+  if (!known) return set_error(BT_EINVAL, "bt_elementwise: unknown op code %d", op);
+  int rc = check_tensor(out, "out", false);
+  if (rc) return rc;
+  for (int k = 0; k < n_in; ++k)
+    if ((rc = check_tensor(&in[k], "input", false))) return rc;
+  const int cdt = attrs->compute_dtype;
+  if (!dtype_valid(cdt)) return set_error(BT_EDTYPE, "bt_elementwise: compute dtype %d", cdt);
+  if (cdt == BT_F16) return set_error(BT_EDTYPE, "bt_elementwise: fp16 is widened to fp32 before compute");
+  const bool float_only = !(op == BT_OP_ADD || op == BT_OP_SUB || op == BT_OP_MUL || op == BT_OP_DIV ||
+                            op == BT_OP_CLIP || op == BT_OP_EQUAL || op == BT_OP_GREATER || op == BT_OP_LESS ||
+                            op == BT_OP_GEQ || op == BT_OP_AND || op == BT_OP_WHERE || op == BT_OP_NEG ||
+                            op == BT_OP_ABS || op == BT_OP_MIN || op == BT_OP_MAX || op == BT_OP_IDENTITY ||
+                            op == BT_OP_CAST_INT || op == BT_OP_CAST_BOOL);
+  if (float_only && !is_float_dtype(cdt))
+    return set_error(BT_EDTYPE, "bt_elementwise: op %d needs a floating compute dtype", op);
+  if ((op == BT_OP_GELU || op == BT_OP_DEQUANT) && cdt != BT_F32)
+    return set_error(BT_EDTYPE, "bt_elementwise: op %d computes in float32 only", op);
+  if (cdt == BT_U64 && op != BT_OP_ADD && op != BT_OP_SUB && op != BT_OP_MUL && op != BT_OP_IDENTITY &&
+      op != BT_OP_CAST_INT && op != BT_OP_CAST_BOOL && op != BT_OP_EQUAL)
+    return set_error(BT_EUNSUPPORTED, "bt_elementwise: uint64 compute supports add/sub/mul/equal/casts only");
+
+  const bt_tensor* ops[4];
+  for (int k = 0; k < n_in; ++k) ops[k] = &in[k];
+  ops[n_in] = out;
+  BcastPlan p;
+  if ((rc = plan_broadcast(n_in + 1, ops, out->shape, out->rank, &p))) return rc;
+  if (p.n == 0) return BT_OK;
+
+  EwArgs a{};
+  a.op = op; a.n_in = n_in; a.rank = p.rank; a.cdt = cdt; a.alpha = attrs->alpha; a.odt = out->dtype;
+  a.n = p.n;
+  for (int d = 0; d < p.rank; ++d) a.shape[d] = p.shape[d];
+  for (int k = 0; k < 3; ++k) {
+    const int src = k < n_in ? k : 0;
+    a.in[k].p = in[src].data;
+    a.in[k].dt = in[src].dtype;
+    for (int d = 0; d < BT_MAX_RANK; ++d) a.in[k].st[d] = (k < n_in && d < p.rank) ? p.st[k][d] : 0;
+  }
+  a.out = out->data;
+  for (int d = 0; d < BT_MAX_RANK; ++d) a.ost[d] = d < p.rank ? p.st[n_in][d] : 0;
+
+  cudaStream_t s = cur_stream();
+  const int threads = 256;
+  const bool f32_path = (cdt == BT_F32) && op != BT_OP_WHERE && op != BT_OP_AND;
+  if (f32_path && p.rank == 1 && a.ost[0] == 1) {
+    bool unit = true, vec_ok = aligned_run(out->data, out->dtype, 4);
+    for (int k = 0; k < n_in; ++k) {
+      if (a.in[k].st[0] != 0 && a.in[k].st[0] != 1) unit = false;
+      if (a.in[k].st[0] == 1 && !aligned_run(a.in[k].p, a.in[k].dt, 4)) vec_ok = false;
+    }
+    if (unit) {
+      if (vec_ok) ew_flat_kernel<4><<<grid_for((a.n + 3) / 4, threads), threads, 0, s>>>(a);
+      else ew_flat_kernel<1><<<grid_for(a.n, threads), threads, 0, s>>>(a);
+      return check_launch("bt_elementwise(flat)");
+    }
+  }
+  if (f32_path && p.rank == 2 && a.ost[1] == 1) {
+    bool ok = true, vec_ok = (p.shape[1] % 4 == 0) && aligned_run(out->data, out->dtype, 4) && (a.ost[0] % 4 == 0);
+    for (int k = 0; k < n_in; ++k) {
+      if (a.in[k].st[1] != 0 && a.in[k].st[1] != 1) ok = false;
+      if (a.in[k].st[1] == 1 && (a.in[k].st[0] % 4 != 0 || !aligned_run(a.in[k].p, a.in[k].dt, 4))) vec_ok = false;
+    }
+    if (ok) {
+      const int vec = vec_ok ? 4 : 1;
+      int64_t per_row = (p.shape[1] / vec + threads - 1) / threads;
+      if (per_row < 1) per_row = 1;
+      int gy = (int)(p.shape[0] < 65535 ? p.shape[0] : 65535);
+      int gx = (int)(per_row > 64 ? 64 : per_row);
+      dim3 grid(gx, gy);
+      if (vec_ok) ew_rows_kernel<4><<<grid, threads, 0, s>>>(a);
+      else ew_rows_kernel<1><<<grid, threads, 0, s>>>(a);
+      return check_launch("bt_elementwise(rows)");
+    }
+  }
+  const int g = grid_for(a.n, threads);
+  switch (cdt) {
+    case BT_F32: ew_nd_kernel<float><<<g, threads, 0, s>>>(a); break;
+    case BT_F64: ew_nd_kernel<double><<<g, threads, 0, s>>>(a); break;
+    default: ew_nd_kernel<long long><<<g, threads, 0, s>>>(a); break;
+  }
+  return check_launch("bt_elementwise(nd)");
+}
+
+extern "C" int bt_fused_chain(const bt_chain* prog, const bt_tensor* in, const bt_tensor* out) {
+  if (!prog || !in || !out) return set_error(BT_EINVAL, "bt_fused_chain: null argument");
+  if (prog->n_in < 1 || prog->n_in > BT_CHAIN_MAX_IN)
+    return set_error(BT_EINVAL, "bt_fused_chain: n_in %d outside 1..%d", prog->n_in, BT_CHAIN_MAX_IN);
+  if (prog->n_instr < 0 || prog->n_instr > BT_CHAIN_MAX_INSTR)
+    return set_error(BT_EINVAL, "bt_fused_chain: %d instructions (max %d)", prog->n_instr, BT_CHAIN_MAX_INSTR);
+  if (prog->out_reg < 0 || prog->out_reg >= kChainRegs)
+    return set_error(BT_EINVAL, "bt_fused_chain: output register %d", prog->out_reg);
+  for (int k = 0; k < prog->n_instr; ++k) {
+    const bt_chain_instr& ins = prog->instr[k];
+    if (ins.dst < 0 || ins.dst >= kChainRegs || ins.a < 0 || ins.a >= kChainRegs || ins.b < 0 || ins.b >= kChainRegs)
+      return set_error(BT_EINVAL, "bt_fused_chain: instruction %d uses a register outside 0..%d", k, kChainRegs - 1);
+    if (ins.op < 0 || ins.op > 31 || ins.op == BT_OP_WHERE || ins.op == BT_OP_AND || ins.op == BT_OP_CLIP)
+      return set_error(BT_EINVAL, "bt_fused_chain: instruction %d has op %d", k, ins.op);
+  }
+  int rc = check_tensor(out, "out", false);
+  if (rc) return rc;
+  const bt_tensor* ops[BT_CHAIN_MAX_IN + 1];
+  for (int k = 0; k < prog->n_in; ++k) {
+    if ((rc = check_tensor(&in[k], "input", false))) return rc;
+    if (in[k].dtype == BT_F64 || in[k].dtype == BT_I64 || in[k].dtype == BT_U64)
+      return set_error(BT_EDTYPE, "bt_fused_chain: 64-bit inputs are not widened to float32 exactly");
+  }
+  // The planner merges at most 4 operands at a time; broadcast each input
+  // against the output separately, then merge axes across all of them.
+  ChainArgs a{};
+  a.prog = *prog;
+  a.odt = out->dtype;
+  int R = out->rank;
+  int64_t n = 1;
+  for (int d = 0; d < R; ++d) { a.shape[d] = out->shape[d]; n *= out->shape[d]; }
+  a.n = n;
+  if (n == 0) return BT_OK;
+  for (int k = 0; k < prog->n_in; ++k) {
+    const bt_tensor* t = &in[k];
+    if (t->rank > R) return set_error(BT_ESHAPE, "bt_fused_chain: input %d rank %d > output rank %d", k, t->rank, R);
+    int pad = R - t->rank;
+    for (int d = 0; d < R; ++d) {
+      if (d < pad) { a.st[k][d] = 0; continue; }
+      int64_t e = t->shape[d - pad];
+      if (e == out->shape[d]) a.st[k][d] = e == 1 ? 0 : t->strides[d - pad];
+      else if (e == 1) a.st[k][d] = 0;
+      else return set_error(BT_ESHAPE, "bt_fused_chain: input %d does not broadcast on axis %d", k, d);
+    }
+    a.p[k] = t->data;
+    a.dt[k] = t->dtype;
+  }
+  for (int d = 0; d < R; ++d) a.ost[d] = out->shape[d] == 1 ? 0 : out->strides[d];
+  // merge contiguous axes (all operands and the output)
+  int r = 0;
+  int64_t dims[BT_MAX_RANK], st[BT_CHAIN_MAX_IN + 1][BT_MAX_RANK];
+  for (int d = 0; d < R; ++d) {
+    if (a.shape[d] == 1) continue;
+    dims[r] = a.shape[d];
+    for (int k = 0; k < prog->n_in; ++k) st[k][r] = a.st[k][d];
+    st[prog->n_in][r] = a.ost[d];
+    ++r;
+  }
+  for (int i = r - 1; i > 0; --i) {
+    bool ok = true;
+    for (int k = 0; k <= prog->n_in; ++k)
+      if (st[k][i - 1] != st[k][i] * dims[i]) { ok = false; break; }
+    if (!ok) continue;
+    dims[i - 1] *= dims[i];
+    for (int k = 0; k <= prog->n_in; ++k) st[k][i - 1] = st[k][i];
+    for (int j = i; j < r - 1; ++j) {
+      dims[j] = dims[j + 1];
+      for (int k = 0; k <= prog->n_in; ++k) st[k][j] = st[k][j + 1];
+    }
+    --r;
+  }
+  if (r == 0) { dims[0] = 1; for (int k = 0; k <= prog->n_in; ++k) st[k][0] = 0; r = 1; }
+  a.rank = r;
+  for (int d = 0; d < BT_MAX_RANK; ++d) {
+    a.shape[d] = d < r ? dims[d] : 1;
+    for (int k = 0; k < BT_CHAIN_MAX_IN; ++k) a.st[k][d] = (k < prog->n_in && d < r) ? st[k][d] : 0;
+    a.ost[d] = d < r ? st[prog->n_in][d] : 0;
+  }
+  (void)ops;
+  const int threads = 256;
+  chain_kernel<<<grid_for(a.n, threads), threads, 0, cur_stream()>>>(a);
+  return check_launch("bt_fused_chain");
+}

@@ -1,0 +1,48 @@
+// bt_internal.h -- host-side plumbing shared by the library's translation
+// units: error reporting, the per-thread stream, device properties, tensor
+// validation and the broadcast planner's result type.
+#pragma once
+#include <stdint.h>
+#include <cuda_runtime.h>
+#include "bt_ops.h"
+
+namespace bt {
+
+// Records a message for bt_last_error() on the calling thread; returns code.
+int set_error(int code, const char* fmt, ...);
+// Stream chosen with bt_set_stream() on the calling thread.
+cudaStream_t cur_stream();
+// Converts a pending CUDA error (launch failure) into BT_ECUDA.
+int check_launch(const char* what);
+
+struct DevInfo {
+  int device = -1;
+  int sm_count = 0;
+  int max_smem_optin = 0;   // bytes per block with the opt-in attribute
+  int max_threads_per_sm = 0;
+};
+// Properties of the calling thread's current device (cached).
+int dev_info(DevInfo* out);
+
+int dtype_size(int dt);
+bool dtype_valid(int dt);
+bool is_float_dtype(int dt);
+// Validates pointer, dtype and rank of a tensor view; name is used in errors.
+int check_tensor(const bt_tensor* t, const char* name, bool allow_null_data);
+int64_t numel(const bt_tensor* t);
+bool is_contiguous(const bt_tensor* t);
+
+// Result of broadcasting n operand views to an output shape and merging the
+// axes every operand walks contiguously.
+struct BcastPlan {
+  int rank = 0;                       // >= 1
+  int64_t shape[BT_MAX_RANK];
+  int64_t st[4][BT_MAX_RANK];         // per operand (inputs..., output last)
+  int64_t n = 0;                      // total elements
+};
+// ops[0..n_ops) are the operands (inputs then output); all broadcast to
+// out_shape (rank out_rank).
+int plan_broadcast(int n_ops, const bt_tensor* const* ops,
+                   const int64_t* out_shape, int out_rank, BcastPlan* p);
+
+}  // namespace bt

@@ -1,0 +1,781 @@
+// bt_rows.cu -- row kernels for sm_100a: reductions, softmax, (skip) layer
+// normalisation and the fused AdaIN1d -> Snake of the Kokoro generator.
+//
+// Layout: one CTA owns one row of T contiguous fp32 values.  The row is
+// staged once from HBM into shared memory (128-bit loads over the 16-byte
+// aligned middle of the row, the shared buffer offset so the phases match),
+// every statistic is computed from shared memory, and the outputs are
+// streamed back with 128-bit stores.  HBM therefore sees each input byte once
+// and each output byte once -- the algorithmic minimum -- while the
+// statistics keep numpy's exact two-pass order.
+//
+// numpy order.  np.add.reduce over a contiguous float32 axis is numpy's
+// pairwise summation (bt_core.h).  Its tree depends on T only, so each CTA
+// first lays the tree out in shared memory (heap numbering: node h has
+// children 2h and 2h+1; kind 0 = absent, 1 = leaf of <= 128 values,
+// 2 = inner node), then sums all leaves in parallel (8 lanes per leaf, one
+// lane per numpy accumulator, combined by shuffles in numpy's bracket order)
+// and finally combines the inner nodes level by level.  The result is
+// bit-identical to numpy for any T.  Means divide the float32 sum by the
+// count in double precision, as np.mean does.
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <atomic>
+#include "bt_ops.h"
+#include "bt_internal.h"
+#include "bt_core.h"
+
+namespace bt {
+namespace {
+
+constexpr int kMaxRow = 49152;   // longest row one CTA stages (192 KiB fp32)
+
+// ---- pairwise plan -----------------------------------------------------------
+struct PwPlan {
+  unsigned char* kind;   // [2 << depth]
+  float* hsum;           // [2 << depth]
+  int* leaf_off;         // [1 << depth]
+  short* leaf_len;
+  short* leaf_id;
+  int* n_leaf;           // counter in shared memory
+  int depth;
+};
+
+// Shared-memory bytes the plan of depth D needs (after the row buffer).
+__host__ __device__ inline size_t plan_bytes(int D) {
+  size_t ids = (size_t)2 << D, leaves = (size_t)1 << D;
+  return ids * sizeof(float) + leaves * sizeof(int) + ids + 2 * leaves * sizeof(short) + 16;
+}
+
+__device__ inline PwPlan plan_at(unsigned char* base, int D) {
+  PwPlan P;
+  size_t ids = (size_t)2 << D, leaves = (size_t)1 << D;
+  P.hsum = (float*)base;
+  P.leaf_off = (int*)(base + ids * sizeof(float));
+  P.n_leaf = (int*)(base + ids * sizeof(float) + leaves * sizeof(int));
+  P.kind = base + ids * sizeof(float) + leaves * sizeof(int) + 16;
+  P.leaf_len = (short*)(P.kind + ids);
+  P.leaf_id = P.leaf_len + leaves;
+  P.depth = D;
+  return P;
+}
+
+// Lays out numpy's pairwise tree for a run of n values (whole CTA).
+__device__ void pw_build(PwPlan& P, int n) {
+  if (threadIdx.x == 0) *P.n_leaf = 0;
+  __syncthreads();
+  const int ids = 2 << P.depth;
+  for (int h = threadIdx.x + 1; h < ids; h += blockDim.x) {
+    const int k = 31 - __clz(h);
+    int lo = 0, len = n;
+    bool exists = true;
+    for (int b = k - 1; b >= 0; --b) {
+      if (len <= kPwLeaf) { exists = false; break; }
+      const int h2 = (int)pw_split(len);
+      if ((h >> b) & 1) { lo += h2; len -= h2; } else { len = h2; }
+    }
+    unsigned char kd = 0;
+    if (exists) kd = (len <= kPwLeaf) ? 1 : 2;
+    P.kind[h] = kd;
+    if (kd == 1) {
+      const int pos = atomicAdd(P.n_leaf, 1);
+      P.leaf_off[pos] = lo;
+      P.leaf_len[pos] = (short)len;
+      P.leaf_id[pos] = (short)h;
+    }
+  }
+  __syncthreads();
+}
+
+// numpy's pairwise sum of f(s[0..n)) with the plan in P (whole CTA; every
+// thread receives the result).  SQUARE selects f(v) = v*v.
+template <bool SQUARE>
+__device__ float pw_sum(const float* s, PwPlan& P) {
+  const int lane8 = threadIdx.x & 7;
+  const int grp = threadIdx.x >> 3, ngrp = blockDim.x >> 3;
+  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+  const int nl = *P.n_leaf;
+  for (int L = grp; L < nl; L += ngrp) {
+    const int off = P.leaf_off[L], len = P.leaf_len[L];
+    float res;
+    if (len < 8) {
+      res = 0.0f;
+      if (lane8 == 0)
+        for (int i = 0; i < len; ++i) {
+          float v = s[off + i];
+          res = BT_ADD(res, SQUARE ? BT_MUL(v, v) : v);
+        }
+    } else {
+      float v = s[off + lane8];
+      float r = SQUARE ? BT_MUL(v, v) : v;
+      const int full = len - (len & 7);
+      for (int i = 8; i < full; i += 8) {
+        v = s[off + i + lane8];
+        r = BT_ADD(r, SQUARE ? BT_MUL(v, v) : v);
+      }
+      // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); float addition commutes, so
+      // xor partners reproduce numpy's brackets exactly.
+      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 1));
+      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 2));
+      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 4));
+      res = r;
+      if (lane8 == 0)
+        for (int i = full; i < len; ++i) {
+          v = s[off + i];
+          res = BT_ADD(res, SQUARE ? BT_MUL(v, v) : v);
+        }
+    }
+    if (lane8 == 0) P.hsum[P.leaf_id[L]] = res;
+  }
+  __syncthreads();
+  for (int k = P.depth - 1; k >= 0; --k) {
+    for (int j = threadIdx.x; j < (1 << k); j += blockDim.x) {
+      const int h = (1 << k) + j;
+      if (P.kind[h] == 2) P.hsum[h] = BT_ADD(P.hsum[2 * h], P.hsum[2 * h + 1]);
+    }
+    __syncthreads();
+  }
+  const float total = P.hsum[1];
+  __syncthreads();  // P may be reused by the caller's next sum
+  return total;
+}
+
+// np.max-style block maximum (NaN propagates).
+__device__ float block_max(const float* s, int n, float* red) {
+  float m = -INFINITY;
+  bool nan = false;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = s[i];
+    if (v != v) nan = true;
+    m = fmaxf(m, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
+  }
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = nan ? qnan() : m;
+  __syncthreads();
+  float r = -INFINITY;
+  bool rn = false;
+  for (int i = 0; i < nw; ++i) { float v = red[i]; if (v != v) rn = true; r = fmaxf(r, v); }
+  __syncthreads();
+  return rn ? qnan() : r;
+}
+
+// ---- row staging --------------------------------------------------------------
+__device__ __forceinline__ int phase4(const void* p) { return (int)(((uintptr_t)p >> 2) & 3); }
+
+// First element index at which g is 16-byte aligned, and the number of
+// 4-element vectors after it.
+struct RowSplit { int head, nvec; };
+__device__ __forceinline__ RowSplit row_split(const float* g, int n) {
+  RowSplit r;
+  r.head = (4 - phase4(g)) & 3;
+  if (r.head > n) r.head = n;
+  r.nvec = (n - r.head) / 4;
+  return r;
+}
+
+// s[i] = g0[i] (+ g1[i] (+ g2[i])) for i < n; optionally also res[i] = s[i].
+// s must share g0's 16-byte phase.  Sources with another phase, and the
+// residual output when its phase differs, fall back to scalar accesses.
+__device__ void stage_row(float* s, const float* g0, const float* g1, const float* g2, int n, float* res) {
+  const RowSplit sp = row_split(g0, n);
+  const bool v1 = g1 && phase4(g1) == phase4(g0);
+  const bool v2 = g2 && phase4(g2) == phase4(g0);
+  const bool vr = res && phase4(res) == phase4(g0);
+  for (int i = threadIdx.x; i < sp.head; i += blockDim.x) {
+    float v = g0[i];
+    if (g1) v = BT_ADD(v, g1[i]);
+    if (g2) v = BT_ADD(v, g2[i]);
+    s[i] = v;
+    if (res) res[i] = v;
+  }
+  for (int q = threadIdx.x; q < sp.nvec; q += blockDim.x) {
+    const int i = sp.head + 4 * q;
+    float4 v = __ldcs((const float4*)(g0 + i));
+    if (g1) {
+      float4 w = v1 ? __ldcs((const float4*)(g1 + i)) : make_float4(g1[i], g1[i + 1], g1[i + 2], g1[i + 3]);
+      v.x = BT_ADD(v.x, w.x); v.y = BT_ADD(v.y, w.y); v.z = BT_ADD(v.z, w.z); v.w = BT_ADD(v.w, w.w);
+    }
+    if (g2) {
+      float4 w = v2 ? __ldcs((const float4*)(g2 + i)) : make_float4(g2[i], g2[i + 1], g2[i + 2], g2[i + 3]);
+      v.x = BT_ADD(v.x, w.x); v.y = BT_ADD(v.y, w.y); v.z = BT_ADD(v.z, w.z); v.w = BT_ADD(v.w, w.w);
+    }
+    *(float4*)(s + i) = v;
+    if (res) {
+      if (vr) __stcs((float4*)(res + i), v);
+      else { res[i] = v.x; res[i + 1] = v.y; res[i + 2] = v.z; res[i + 3] = v.w; }
+    }
+  }
+  for (int i = sp.head + 4 * sp.nvec + threadIdx.x; i < n; i += blockDim.x) {
+    float v = g0[i];
+    if (g1) v = BT_ADD(v, g1[i]);
+    if (g2) v = BT_ADD(v, g2[i]);
+    s[i] = v;
+    if (res) res[i] = v;
+  }
+}
+
+// Shared row buffer aligned to g's 16-byte phase.
+__device__ __forceinline__ float* row_buffer(unsigned char* smem, const void* g) {
+  return (float*)smem + phase4(g);
+}
+
+// Dynamic shared memory layout: [row buffer: n + 4 floats][32 floats][plan].
+__host__ __device__ inline size_t row_smem_bytes(int n, int D) {
+  size_t rowb = ((size_t)n + 4) * sizeof(float);
+  rowb = (rowb + 15) & ~(size_t)15;
+  return rowb + 32 * sizeof(float) + plan_bytes(D);
+}
+__device__ inline float* red_area(unsigned char* smem, int n) {
+  size_t rowb = (((size_t)n + 4) * sizeof(float) + 15) & ~(size_t)15;
+  return (float*)(smem + rowb);
+}
+__device__ inline unsigned char* plan_area(unsigned char* smem, int n) {
+  return (unsigned char*)(red_area(smem, n) + 32);
+}
+
+// ---- kernels ---------------------------------------------------------------------
+struct ReduceRowsArgs {
+  const void* x;
+  int32_t xdt;        // BT_F32 or BT_F16 (widened exactly)
+  int32_t mean;
+  int32_t n, depth;
+  int64_t rows;
+  float* out;
+};
+
+__global__ void reduce_rows_kernel(ReduceRowsArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int n = a.n;
+  PwPlan P = plan_at(plan_area(smem, n), a.depth);
+  pw_build(P, n);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    float* s;
+    if (a.xdt == BT_F32) {
+      const float* g = (const float*)a.x + row * (int64_t)n;
+      s = row_buffer(smem, g);
+      stage_row(s, g, nullptr, nullptr, n, nullptr);
+    } else {
+      const __half* g = (const __half*)a.x + row * (int64_t)n;
+      s = (float*)smem;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = __half2float(g[i]);
+    }
+    __syncthreads();
+    const float sum = BT_ADD(0.0f, pw_sum<false>(s, P));
+    if (threadIdx.x == 0) a.out[row] = a.mean ? np_mean_from_sum(sum, n) : sum;
+  }
+}
+
+// Reduction of the middle axis of a contiguous [O, R, I] view: numpy adds the
+// R slices one after another into the output (its inner loop runs along I).
+struct ReduceColsArgs {
+  const void* x;
+  int32_t xdt;
+  int32_t mean;
+  int64_t O, R, I;
+  float* out;
+};
+__global__ void reduce_cols_kernel(ReduceColsArgs a) {
+  const int64_t total = a.O * a.I;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t o = idx / a.I, i = idx - o * a.I;
+    int64_t p = o * a.R * a.I + i;
+    float acc = 0.0f;
+    if (a.xdt == BT_F32) {
+      const float* x = (const float*)a.x;
+      for (int64_t r = 0; r < a.R; ++r, p += a.I) acc = BT_ADD(acc, __ldg(x + p));
+    } else {
+      const __half* x = (const __half*)a.x;
+      for (int64_t r = 0; r < a.R; ++r, p += a.I) acc = BT_ADD(acc, __half2float(x[p]));
+    }
+    a.out[idx] = a.mean ? np_mean_from_sum(acc, a.R) : acc;
+  }
+}
+
+struct SoftmaxArgs {
+  const float* x;
+  const float* mask;                 // may be null
+  int32_t n, depth;
+  int64_t rows;
+  int32_t lead_rank;                 // rank of x's leading (row) axes
+  int64_t lead_shape[BT_MAX_RANK];
+  int64_t mask_lead_st[BT_MAX_RANK]; // mask stride per leading axis (0 = broadcast)
+  int64_t mask_col_st;               // mask stride along the softmax axis (0 or 1)
+  float* out;
+};
+
+__global__ void softmax_rows_kernel(SoftmaxArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int n = a.n;
+  PwPlan P = plan_at(plan_area(smem, n), a.depth);
+  float* red = red_area(smem, n);
+  pw_build(P, n);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const float* g = a.x + row * (int64_t)n;
+    float* s = row_buffer(smem, g);
+    stage_row(s, g, nullptr, nullptr, n, nullptr);
+    if (a.mask) {
+      __syncthreads();
+      int64_t rem = row, moff = 0;
+      for (int d = a.lead_rank - 1; d >= 0; --d) {
+        const int64_t c = rem % a.lead_shape[d];
+        rem /= a.lead_shape[d];
+        moff += c * a.mask_lead_st[d];
+      }
+      for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_ADD(s[i], a.mask[moff + i * a.mask_col_st]);
+    }
+    __syncthreads();
+    const float m = block_max(s, n, red);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = np_expf(BT_SUB(s[i], m));
+    __syncthreads();
+    const float denom = BT_ADD(0.0f, pw_sum<false>(s, P));
+    float* o = a.out + row * (int64_t)n;
+    const RowSplit sp = row_split(o, n);
+    const bool vec = phase4(o) == phase4(g);
+    if (vec) {
+      for (int i = threadIdx.x; i < sp.head; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+      for (int q = threadIdx.x; q < sp.nvec; q += blockDim.x) {
+        const int i = sp.head + 4 * q;
+        float4 v = *(const float4*)(s + i);
+        __stcs((float4*)(o + i), make_float4(BT_DIV(v.x, denom), BT_DIV(v.y, denom), BT_DIV(v.z, denom), BT_DIV(v.w, denom)));
+      }
+      for (int i = sp.head + 4 * sp.nvec + threadIdx.x; i < n; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+    }
+    __syncthreads();
+  }
+}
+
+struct LayerNormArgs {
+  const float* x;
+  const float* skip;      // [rows, n] or null
+  const float* bias;      // [n] or null (added after skip)
+  const void* gamma;      // [n]
+  const void* beta;       // [n] or null
+  int32_t gdt, bdt;       // dtypes of gamma / beta (F32 or F16)
+  int32_t n, depth;
+  int64_t rows;
+  float eps;
+  float* out;
+};
+
+__device__ __forceinline__ float ldf(const void* p, int dt, int64_t i) {
+  return dt == BT_F16 ? __half2float(((const __half*)p)[i]) : ((const float*)p)[i];
+}
+
+__global__ void layernorm_rows_kernel(LayerNormArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int n = a.n;
+  PwPlan P = plan_at(plan_area(smem, n), a.depth);
+  pw_build(P, n);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const float* g = a.x + row * (int64_t)n;
+    float* s = row_buffer(smem, g);
+    stage_row(s, g, a.skip ? a.skip + row * (int64_t)n : nullptr, nullptr, n, nullptr);
+    if (a.bias) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_ADD(s[i], a.bias[i]);
+    }
+    __syncthreads();
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum<false>(s, P)), n);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_SUB(s[i], mu);
+    __syncthreads();
+    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum<true>(s, P)), n);
+    const float sd = BT_SQRT(BT_ADD(var, a.eps));
+    float* o = a.out + row * (int64_t)n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float y = BT_MUL(BT_DIV(s[i], sd), ldf(a.gamma, a.gdt, i));
+      if (a.beta) y = BT_ADD(y, ldf(a.beta, a.bdt, i));
+      o[i] = y;
+    }
+    __syncthreads();
+  }
+}
+
+struct AdainArgs {
+  bt_adain_args p;
+  int32_t depth;
+  int32_t n;
+};
+
+__global__ void adain_snake_kernel(AdainArgs A) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const bt_adain_args& a = A.p;
+  const int n = A.n;
+  PwPlan P = plan_at(plan_area(smem, n), A.depth);
+  pw_build(P, n);
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * (int64_t)n;
+    const float* g0 = a.src[0] + base;
+    float* s = row_buffer(smem, g0);
+    stage_row(s, g0, a.n_src > 1 ? a.src[1] + base : nullptr, a.n_src > 2 ? a.src[2] + base : nullptr, n,
+              a.res ? a.res + base : nullptr);
+    __syncthreads();
+    // ReduceMean -> Sub -> Mul(d, d) -> ReduceMean -> Add eps -> Sqrt
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum<false>(s, P)), n);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_SUB(s[i], mu);
+    __syncthreads();
+    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum<true>(s, P)), n);
+    const float sd = BT_SQRT(BT_ADD(var, a.eps));
+    const int64_t c = row % a.channels, b = row / a.channels;
+    const RowSplit sp = row_split(g0, n);
+    for (int k = 0; k < a.n_out; ++k) {
+      const float gain = a.gain[k][b * a.gain_stride + c], shift = a.shift[k][b * a.shift_stride + c];
+      const bool snake = a.alpha[k] != nullptr;
+      float al = 0.f, ial = 0.f;
+      if (snake) {
+        al = ldf(a.alpha[k], a.alpha_dtype, c);
+        ial = ldf(a.inv_alpha[k], a.alpha_dtype, c);
+      }
+      float* o = a.out[k] + base;
+      // Div -> Mul(1+gamma) -> Add(beta) [-> Mul(alpha) -> Sin -> Pow 2 -> Mul(1/alpha) -> Add]
+      auto f = [&](float d) -> float {
+        float y = BT_ADD(BT_MUL(gain, BT_DIV(d, sd)), shift);
+        if (!snake) return y;
+        const float t = np_sinf(BT_MUL(al, y));
+        return BT_ADD(y, BT_MUL(ial, BT_MUL(t, t)));
+      };
+      if (phase4(o) == phase4(g0)) {
+        for (int i = threadIdx.x; i < sp.head; i += blockDim.x) o[i] = f(s[i]);
+        for (int q = threadIdx.x; q < sp.nvec; q += blockDim.x) {
+          const int i = sp.head + 4 * q;
+          const float4 d = *(const float4*)(s + i);
+          __stcs((float4*)(o + i), make_float4(f(d.x), f(d.y), f(d.z), f(d.w)));
+        }
+        for (int i = sp.head + 4 * sp.nvec + threadIdx.x; i < n; i += blockDim.x) o[i] = f(s[i]);
+      } else {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = f(s[i]);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+struct MeanLeakyArgs {
+  const float* a[3];
+  const float* b[3];
+  int64_t n;
+  float divisor, slope;
+  float* out;
+};
+
+__device__ __forceinline__ float mean_leaky(float a0, float b0, float a1, float b1, float a2, float b2,
+                                            float div, float slope) {
+  float v = BT_ADD(BT_ADD(BT_ADD(a0, b0), BT_ADD(a1, b1)), BT_ADD(a2, b2));
+  v = BT_DIV(v, div);
+  return v < 0.0f ? BT_MUL(v, slope) : v;
+}
+
+__global__ void __launch_bounds__(256) mean_leaky_kernel(MeanLeakyArgs m) {
+  const int64_t nv = m.n / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
+    const int64_t i = 4 * v;
+    float4 x[6];
+    x[0] = __ldcs((const float4*)(m.a[0] + i)); x[1] = __ldcs((const float4*)(m.b[0] + i));
+    x[2] = __ldcs((const float4*)(m.a[1] + i)); x[3] = __ldcs((const float4*)(m.b[1] + i));
+    x[4] = __ldcs((const float4*)(m.a[2] + i)); x[5] = __ldcs((const float4*)(m.b[2] + i));
+    float4 r;
+    r.x = mean_leaky(x[0].x, x[1].x, x[2].x, x[3].x, x[4].x, x[5].x, m.divisor, m.slope);
+    r.y = mean_leaky(x[0].y, x[1].y, x[2].y, x[3].y, x[4].y, x[5].y, m.divisor, m.slope);
+    r.z = mean_leaky(x[0].z, x[1].z, x[2].z, x[3].z, x[4].z, x[5].z, m.divisor, m.slope);
+    r.w = mean_leaky(x[0].w, x[1].w, x[2].w, x[3].w, x[4].w, x[5].w, m.divisor, m.slope);
+    __stcs((float4*)(m.out + i), r);
+  }
+  for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m.n; i += stride)
+    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.divisor, m.slope);
+}
+
+__global__ void mean_leaky_scalar_kernel(MeanLeakyArgs m) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m.n; i += stride)
+    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.divisor, m.slope);
+}
+
+// ---- launch helpers ----------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_smem_ready[kMaxDevices];
+
+int raise_smem_limits() {
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  if (di.device >= kMaxDevices) return set_error(BT_EUNSUPPORTED, "device ordinal %d >= %d", di.device, kMaxDevices);
+  if (g_smem_ready[di.device].load()) return BT_OK;
+  const void* fns[] = {(const void*)reduce_rows_kernel, (const void*)softmax_rows_kernel,
+                       (const void*)layernorm_rows_kernel, (const void*)adain_snake_kernel};
+  for (const void* f : fns) {
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, di.max_smem_optin);
+    if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  g_smem_ready[di.device].store(1);
+  return BT_OK;
+}
+
+int row_threads(int n) {
+  if (n <= 1024) return 128;
+  if (n <= 8192) return 256;
+  return 512;
+}
+
+int row_launch_check(int n, size_t* smem, int* depth) {
+  if (n > kMaxRow)
+    return set_error(BT_ETOOBIG, "row of %d values exceeds the %d-value limit of one CTA", n, kMaxRow);
+  int rc = raise_smem_limits();
+  if (rc) return rc;
+  *depth = pw_depth(n);
+  *smem = row_smem_bytes(n, *depth);
+  DevInfo di;
+  dev_info(&di);
+  if ((int64_t)*smem > di.max_smem_optin)
+    return set_error(BT_ETOOBIG, "row needs %zu bytes of shared memory (device allows %d)", *smem, di.max_smem_optin);
+  return BT_OK;
+}
+
+int row_grid(int64_t rows) {
+  int64_t g = rows < 1 ? 1 : rows;
+  if (g > 2147483647) g = 2147483647;
+  return (int)g;
+}
+
+}  // namespace
+}  // namespace bt
+
+using namespace bt;
+
+extern "C" int bt_init(int device) {
+  if (device >= 0) {
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+  }
+  return raise_smem_limits();
+}
+
+extern "C" int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int n_axes, int keepdims,
+                         const bt_tensor* out) {
+  if (kind != BT_REDUCE_SUM && kind != BT_REDUCE_MEAN) return set_error(BT_EINVAL, "bt_reduce: kind %d", kind);
+  int rc = check_tensor(x, "x", false);
+  if (rc) return rc;
+  if ((rc = check_tensor(out, "out", false))) return rc;
+  if (n_axes < 0 || n_axes > x->rank || (n_axes > 0 && !axes)) return set_error(BT_EINVAL, "bt_reduce: bad axes");
+  if (x->dtype != BT_F32 && x->dtype != BT_F16)
+    return set_error(BT_EDTYPE, "bt_reduce: input dtype %d (float32/float16 only)", x->dtype);
+  if (out->dtype != BT_F32) return set_error(BT_EDTYPE, "bt_reduce: output must be float32");
+  if (!is_contiguous(x) || !is_contiguous(out)) return set_error(BT_EUNSUPPORTED, "bt_reduce: contiguous views only");
+  bool red[BT_MAX_RANK] = {false};
+  for (int i = 0; i < n_axes; ++i) {
+    if (axes[i] < 0 || axes[i] >= x->rank) return set_error(BT_EINVAL, "bt_reduce: axis %lld", (long long)axes[i]);
+    if (red[axes[i]]) return set_error(BT_EINVAL, "bt_reduce: repeated axis %lld", (long long)axes[i]);
+    red[axes[i]] = true;
+  }
+  // expected output extent
+  int64_t expect = 1;
+  for (int d = 0; d < x->rank; ++d) if (!red[d]) expect *= x->shape[d];
+  if (numel(out) != expect) return set_error(BT_ESHAPE, "bt_reduce: output has %lld elements, expected %lld",
+                                             (long long)numel(out), (long long)expect);
+  (void)keepdims;
+  // Collapse to [O, R, I]: the reduced axes must be one contiguous block
+  // (after dropping size-1 axes).
+  int first = -1, last = -1;
+  for (int d = 0; d < x->rank; ++d) {
+    if (x->shape[d] == 1) continue;
+    if (red[d]) { if (first < 0) first = d; last = d; }
+  }
+  int64_t O = 1, R = 1, I = 1;
+  for (int d = 0; d < x->rank; ++d) {
+    if (x->shape[d] == 1) continue;
+    if (first >= 0 && d >= first && d <= last) {
+      if (!red[d]) return set_error(BT_EUNSUPPORTED, "bt_reduce: reduced axes must form one contiguous block");
+      R *= x->shape[d];
+    } else if (first >= 0 && d > last) I *= x->shape[d];
+    else O *= x->shape[d];
+  }
+  if (numel(x) == 0 || expect == 0) {
+    if (expect == 0) return BT_OK;
+    // empty reduction: sum 0, mean NaN (numpy's 0/0)
+    return set_error(BT_EUNSUPPORTED, "bt_reduce: empty reduction is handled by the caller");
+  }
+  cudaStream_t s = cur_stream();
+  if (I == 1) {
+    if (R > kMaxRow) return set_error(BT_ETOOBIG, "bt_reduce: reduced run of %lld values exceeds %d", (long long)R, kMaxRow);
+    size_t smem;
+    int depth;
+    if ((rc = row_launch_check((int)R, &smem, &depth))) return rc;
+    ReduceRowsArgs a{x->data, x->dtype, kind == BT_REDUCE_MEAN, (int)R, depth, O, (float*)out->data};
+    reduce_rows_kernel<<<row_grid(O), row_threads((int)R), smem, s>>>(a);
+    return check_launch("bt_reduce(rows)");
+  }
+  ReduceColsArgs a{x->data, x->dtype, kind == BT_REDUCE_MEAN, O, R, I, (float*)out->data};
+  int64_t work = O * I;
+  int g = (int)((work + 255) / 256);
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  reduce_cols_kernel<<<g, 256, 0, s>>>(a);
+  return check_launch("bt_reduce(cols)");
+}
+
+extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, const bt_tensor* out) {
+  int rc = check_tensor(x, "x", false);
+  if (rc) return rc;
+  if ((rc = check_tensor(out, "out", false))) return rc;
+  if (x->dtype != BT_F32 || out->dtype != BT_F32) return set_error(BT_EDTYPE, "bt_softmax: float32 only");
+  if (x->rank < 1) return set_error(BT_ESHAPE, "bt_softmax: rank 0 input");
+  if (axis < 0) axis += x->rank;
+  if (axis != x->rank - 1) return set_error(BT_EUNSUPPORTED, "bt_softmax: last axis only (got %d)", axis);
+  if (!is_contiguous(x) || !is_contiguous(out) || numel(out) != numel(x))
+    return set_error(BT_EUNSUPPORTED, "bt_softmax: contiguous x and out of equal size only");
+  const int64_t n = x->shape[x->rank - 1];
+  const int64_t rows = n ? numel(x) / n : 0;
+  if (rows == 0 || n == 0) return BT_OK;
+  SoftmaxArgs a{};
+  a.x = (const float*)x->data;
+  a.out = (float*)out->data;
+  a.n = (int)n;
+  a.rows = rows;
+  a.lead_rank = x->rank - 1;
+  for (int d = 0; d < a.lead_rank; ++d) a.lead_shape[d] = x->shape[d];
+  if (mask) {
+    if ((rc = check_tensor(mask, "mask", false))) return rc;
+    if (mask->dtype != BT_F32) return set_error(BT_EDTYPE, "bt_softmax: mask must be float32");
+    if (mask->rank > x->rank) return set_error(BT_ESHAPE, "bt_softmax: mask rank exceeds x rank");
+    const int pad = x->rank - mask->rank;
+    for (int d = 0; d < x->rank; ++d) {
+      int64_t e = d < pad ? 1 : mask->shape[d - pad];
+      int64_t st = (d < pad || e == 1) ? 0 : mask->strides[d - pad];
+      if (e != 1 && e != x->shape[d]) return set_error(BT_ESHAPE, "bt_softmax: mask does not broadcast on axis %d", d);
+      if (d < a.lead_rank) a.mask_lead_st[d] = st;
+      else a.mask_col_st = st;
+    }
+    a.mask = (const float*)mask->data;
+  }
+  size_t smem;
+  int depth;
+  if ((rc = row_launch_check((int)n, &smem, &depth))) return rc;
+  a.depth = depth;
+  softmax_rows_kernel<<<row_grid(rows), row_threads((int)n), smem, cur_stream()>>>(a);
+  return check_launch("bt_softmax");
+}
+
+extern "C" int bt_layernorm(const bt_tensor* x, const bt_tensor* skip, const bt_tensor* bias, const bt_tensor* gamma,
+                            const bt_tensor* beta, int axis, float eps, const bt_tensor* out) {
+  int rc = check_tensor(x, "x", false);
+  if (rc) return rc;
+  if ((rc = check_tensor(out, "out", false))) return rc;
+  if ((rc = check_tensor(gamma, "gamma", false))) return rc;
+  if (x->dtype != BT_F32 || out->dtype != BT_F32) return set_error(BT_EDTYPE, "bt_layernorm: float32 x/out only");
+  if (!is_contiguous(x) || !is_contiguous(out) || numel(out) != numel(x))
+    return set_error(BT_EUNSUPPORTED, "bt_layernorm: contiguous x and out of equal size only");
+  if (x->rank < 1) return set_error(BT_ESHAPE, "bt_layernorm: rank 0 input");
+  if (axis < 0) axis += x->rank;
+  if (axis < 0 || axis >= x->rank) return set_error(BT_EINVAL, "bt_layernorm: axis out of range");
+  int64_t n = 1;
+  for (int d = axis; d < x->rank; ++d) n *= x->shape[d];
+  const int64_t rows = n ? numel(x) / n : 0;
+  if (rows == 0 || n == 0) return BT_OK;
+  auto check_vec = [&](const bt_tensor* t, const char* name) -> int {
+    if ((t->dtype != BT_F32 && t->dtype != BT_F16) || numel(t) != n || !is_contiguous(t))
+      return set_error(BT_EUNSUPPORTED, "bt_layernorm: %s must be a contiguous float32/float16 run of %lld values",
+                       name, (long long)n);
+    return BT_OK;
+  };
+  if ((rc = check_vec(gamma, "gamma"))) return rc;
+  LayerNormArgs a{};
+  a.x = (const float*)x->data;
+  a.gamma = gamma->data;
+  a.gdt = gamma->dtype;
+  if (beta) {
+    if ((rc = check_tensor(beta, "beta", false)) || (rc = check_vec(beta, "beta"))) return rc;
+    a.beta = beta->data;
+    a.bdt = beta->dtype;
+  }
+  if (skip) {
+    if ((rc = check_tensor(skip, "skip", false))) return rc;
+    if (skip->dtype != BT_F32 || !is_contiguous(skip) || numel(skip) != numel(x))
+      return set_error(BT_EUNSUPPORTED, "bt_layernorm: skip must be contiguous float32 shaped like x");
+    a.skip = (const float*)skip->data;
+  }
+  if (bias) {
+    if ((rc = check_tensor(bias, "bias", false))) return rc;
+    if (bias->dtype != BT_F32 || numel(bias) != n || !is_contiguous(bias))
+      return set_error(BT_EUNSUPPORTED, "bt_layernorm: bias must be a contiguous float32 run of %lld values", (long long)n);
+    a.bias = (const float*)bias->data;
+  }
+  a.n = (int)n;
+  a.rows = rows;
+  a.eps = eps;
+  a.out = (float*)out->data;
+  size_t smem;
+  int depth;
+  if (n > kMaxRow) return set_error(BT_ETOOBIG, "bt_layernorm: normalised run of %lld values exceeds %d", (long long)n, kMaxRow);
+  if ((rc = row_launch_check((int)n, &smem, &depth))) return rc;
+  a.depth = depth;
+  layernorm_rows_kernel<<<row_grid(rows), row_threads((int)n), smem, cur_stream()>>>(a);
+  return check_launch("bt_layernorm");
+}
+
+extern "C" int bt_adain_snake(const bt_adain_args* p) {
+  if (!p) return set_error(BT_EINVAL, "bt_adain_snake: null argument");
+  if (p->rows < 0 || p->cols < 1 || p->channels < 1)
+    return set_error(BT_EINVAL, "bt_adain_snake: rows %lld cols %lld channels %lld", (long long)p->rows,
+                     (long long)p->cols, (long long)p->channels);
+  if (p->n_src < 1 || p->n_src > BT_ADAIN_MAX_SRC || p->n_out < 1 || p->n_out > BT_ADAIN_MAX_OUT)
+    return set_error(BT_EINVAL, "bt_adain_snake: n_src %d n_out %d", p->n_src, p->n_out);
+  for (int k = 0; k < p->n_src; ++k)
+    if (!p->src[k]) return set_error(BT_EINVAL, "bt_adain_snake: src[%d] is null", k);
+  for (int k = 0; k < p->n_out; ++k) {
+    if (!p->out[k] || !p->gain[k] || !p->shift[k])
+      return set_error(BT_EINVAL, "bt_adain_snake: output %d lacks out/gain/shift", k);
+    if ((p->alpha[k] == nullptr) != (p->inv_alpha[k] == nullptr))
+      return set_error(BT_EINVAL, "bt_adain_snake: output %d has only one of alpha / inv_alpha", k);
+  }
+  if (p->alpha_dtype != BT_F16 && p->alpha_dtype != BT_F32)
+    return set_error(BT_EDTYPE, "bt_adain_snake: alpha dtype %d", p->alpha_dtype);
+  if (p->gain_stride < p->channels || p->shift_stride < p->channels)
+    return set_error(BT_EINVAL, "bt_adain_snake: gain/shift batch strides (%lld, %lld) below C = %lld",
+                     (long long)p->gain_stride, (long long)p->shift_stride, (long long)p->channels);
+  if (p->rows == 0) return BT_OK;
+  if (p->cols > kMaxRow) return set_error(BT_ETOOBIG, "bt_adain_snake: rows of %lld values exceed %d", (long long)p->cols, kMaxRow);
+  size_t smem;
+  int depth, rc;
+  if ((rc = row_launch_check((int)p->cols, &smem, &depth))) return rc;
+  AdainArgs A;
+  A.p = *p;
+  A.depth = depth;
+  A.n = (int)p->cols;
+  adain_snake_kernel<<<row_grid(p->rows), row_threads((int)p->cols), smem, cur_stream()>>>(A);
+  return check_launch("bt_adain_snake");
+}
+
+extern "C" int bt_resblock_mean_leaky(const float* const* a, const float* const* b, int64_t n, float divisor,
+                                      float slope, float* out) {
+  if (!a || !b || !out) return set_error(BT_EINVAL, "bt_resblock_mean_leaky: null argument");
+  MeanLeakyArgs m{};
+  bool vec = ((uintptr_t)out % 16) == 0;
+  for (int k = 0; k < 3; ++k) {
+    if (!a[k] || !b[k]) return set_error(BT_EINVAL, "bt_resblock_mean_leaky: null input %d", k);
+    m.a[k] = a[k];
+    m.b[k] = b[k];
+    if ((uintptr_t)a[k] % 16 || (uintptr_t)b[k] % 16) vec = false;
+  }
+  if (n < 0) return set_error(BT_EINVAL, "bt_resblock_mean_leaky: negative size");
+  if (n == 0) return BT_OK;
+  m.n = n;
+  m.divisor = divisor;
+  m.slope = slope;
+  m.out = out;
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  int64_t blocks = ((vec ? n / 4 : n) + 255) / 256;
+  int64_t cap = (int64_t)di.sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (vec) mean_leaky_kernel<<<(int)blocks, 256, 0, cur_stream()>>>(m);
+  else mean_leaky_scalar_kernel<<<(int)blocks, 256, 0, cur_stream()>>>(m);
+  return check_launch("bt_resblock_mean_leaky");
+}

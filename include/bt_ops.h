@@ -1,0 +1,241 @@
+/*
+ * bt_ops.h -- C ABI of the B200 (sm_100a) tensor-op library for the best-tts
+ * hot path: the elementwise, broadcast, reduction and dequantize ops that the
+ * best-tts graph executor dispatches for Kokoro-82M.
+ *
+ * Every entry point replaces one reference interface, cited beside it as
+ * "replaces:" with file:line into studio-ransom/best-tts-godot:
+ *   - the numpy op table  tools/ref_runtime.py  RefRuntime.dispatch (:428-668),
+ *   - the GDScript executor's GPU dispatchers   runtime/executor.gd,
+ *   - the GLSL kernels                          kernels/*.glsl.
+ *
+ * Conventions
+ *   - Plain C: pointers, sizes, ints.  No exceptions cross the ABI.
+ *   - Every function returns 0 on success or a negative BT_E* code, and then
+ *     bt_last_error() holds a message for the calling thread.
+ *   - The caller owns all device memory.  Tensors are described by bt_tensor
+ *     views: element strides (0 = broadcast along that axis), rank <= 8.
+ *   - Arithmetic follows the reference's numpy semantics: fp16 operands are
+ *     widened to fp32 before use (ref_runtime.py:49-51), broadcasting is
+ *     numpy's right-aligned rule, the output's dtype is the caller's choice
+ *     (numpy's result type) and each op rounds once, in its own dtype.
+ *   - Launches are asynchronous on the stream set with bt_set_stream() for
+ *     the calling thread (default: the legacy default stream) and on the
+ *     calling thread's current CUDA device.
+ *   - Entry points marked "host only" touch no GPU and may be called on a
+ *     machine without one.
+ */
+#ifndef BT_OPS_H
+#define BT_OPS_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BT_ABI_VERSION 1
+#define BT_MAX_RANK 8
+
+/* ---- status codes ------------------------------------------------------ */
+#define BT_OK            0
+#define BT_EINVAL      (-1)   /* bad argument (null pointer, bad code, ...)  */
+#define BT_ESHAPE      (-2)   /* shapes do not broadcast / do not match      */
+#define BT_EDTYPE      (-3)   /* dtype combination not supported             */
+#define BT_ECUDA       (-4)   /* a CUDA runtime call failed                  */
+#define BT_EUNSUPPORTED (-5)  /* valid request outside what is implemented   */
+#define BT_ETOOBIG     (-6)   /* size beyond a documented limit              */
+
+/* ---- element types (numpy dtypes) -------------------------------------- */
+typedef enum bt_dtype {
+  BT_BOOL = 0, BT_I8 = 1, BT_U8 = 2, BT_I16 = 3, BT_U16 = 4, BT_I32 = 5,
+  BT_U32 = 6, BT_I64 = 7, BT_U64 = 8, BT_F16 = 9, BT_F32 = 10, BT_F64 = 11
+} bt_dtype;
+
+/* A strided view of device memory.  `data` points at element [0,...,0]. */
+typedef struct bt_tensor {
+  void*   data;
+  int32_t dtype;                 /* bt_dtype */
+  int32_t rank;                  /* 0 .. BT_MAX_RANK */
+  int64_t shape[BT_MAX_RANK];
+  int64_t strides[BT_MAX_RANK];  /* in elements; 0 means broadcast */
+} bt_tensor;
+
+/* ---- elementwise op codes ----------------------------------------------
+ * Codes 0-31 keep the numbering of the reference's op table
+ * (runtime/ops.gd:12-19, kernels/elementwise.glsl:43-74) so a reference-side
+ * binding can pass its own codes.  CAST_INT / CAST_BOOL / IDENTITY all mean
+ * "convert the (fp16-widened) input to the output's dtype" here, because the
+ * output descriptor carries the target type. */
+typedef enum bt_op {
+  BT_OP_ADD = 0, BT_OP_SUB = 1, BT_OP_MUL = 2, BT_OP_DIV = 3, BT_OP_POW = 4,
+  BT_OP_SQRT = 5, BT_OP_EXP = 6, BT_OP_SIN = 7, BT_OP_COS = 8, BT_OP_ATAN = 9,
+  BT_OP_TANH = 10, BT_OP_SIGMOID = 11, BT_OP_FLOOR = 12, BT_OP_ROUND = 13,
+  BT_OP_LEAKYRELU = 14, BT_OP_CLIP = 15, BT_OP_EQUAL = 16, BT_OP_GREATER = 17,
+  BT_OP_LESS = 18, BT_OP_GEQ = 19, BT_OP_AND = 20, BT_OP_WHERE = 21,
+  BT_OP_CAST_INT = 22, BT_OP_CAST_BOOL = 23, BT_OP_IDENTITY = 24,
+  BT_OP_NEG = 25, BT_OP_ABS = 26, BT_OP_LOG = 27, BT_OP_MIN = 28,
+  BT_OP_MAX = 29, BT_OP_ERF = 30, BT_OP_GELU = 31,
+  /* codes beyond the reference's table */
+  BT_OP_DEQUANT = 40   /* (in0 - in2) * in1, in2 optional (DequantizeLinear) */
+} bt_op;
+
+/* Attributes of an elementwise call. */
+typedef struct bt_ew_attrs {
+  int32_t compute_dtype;   /* dtype the op computes in (numpy result type of
+                              the widened inputs; BT_F32, BT_F64 or an
+                              integer type).  For comparisons: the promoted
+                              type of the operands. */
+  float   alpha;           /* LeakyRelu slope, applied as float32 */
+} bt_ew_attrs;
+
+/* ---- set-up ------------------------------------------------------------ */
+int         bt_abi_version(void);                 /* host only */
+const char* bt_last_error(void);                  /* host only */
+/* Caches the device's properties and raises the shared-memory limits of the
+ * row kernels.  Call once per device (the calling thread's current device is
+ * used if `device` < 0). */
+int         bt_init(int device);
+/* Stream for subsequent launches from the calling thread (cudaStream_t). */
+int         bt_set_stream(void* stream);
+/* Waits for the calling thread's stream; reports asynchronous faults. */
+int         bt_sync(void);
+
+/* ---- elementwise -------------------------------------------------------
+ * out = op(in[0], in[1], in[2]) with numpy broadcasting of every input view
+ * to out->shape.
+ * replaces: ref_runtime.py:446-503 (Add..Where), :572-578 (Cast), :610-611
+ *           (FastGelu), :631-636 (DequantizeLinear);
+ *           executor.gd:678-699 (_ew), :733-827 (_run_gpu op mapping);
+ *           kernels/elementwise.glsl:91-163; kernels/misc.glsl:47-66
+ *           (MODE_UNPACK_F16 / MODE_DEQUANT_I8). */
+int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_tensor* out,
+                   const bt_ew_attrs* attrs);
+
+/* Fused elementwise chain: a short register program evaluated per element of
+ * the broadcast iteration space, each instruction rounding in fp32 as the
+ * separate numpy ops would (no contraction).  Inputs are loaded (fp16/int8/
+ * int32 widened to fp32) into registers r0..r(n_in-1); instruction k writes
+ * register dst.  The output is register `out_reg`.
+ * replaces: chains of ref_runtime.py:446-479 dispatches such as Snake
+ *           (Mul, Sin, Pow 2, Mul, Add) and dequant + gain, each of which the
+ *           reference executes as a separate dispatch with a barrier
+ *           (executor.gd:696-698). */
+#define BT_CHAIN_MAX_INSTR 16
+#define BT_CHAIN_MAX_IN 6
+typedef struct bt_chain_instr {
+  int32_t op;        /* bt_op among ADD SUB MUL DIV POW SQRT EXP SIN COS TANH
+                        SIGMOID LEAKYRELU ERF IDENTITY NEG ABS MIN MAX FLOOR
+                        ROUND ATAN */
+  int32_t dst, a, b; /* register indices (b unused by unary ops) */
+  float   alpha;     /* LeakyRelu slope */
+} bt_chain_instr;
+typedef struct bt_chain {
+  int32_t n_in;
+  int32_t n_instr;
+  int32_t out_reg;
+  bt_chain_instr instr[BT_CHAIN_MAX_INSTR];
+} bt_chain;
+int bt_fused_chain(const bt_chain* prog, const bt_tensor* in,
+                   const bt_tensor* out);
+
+/* ---- reductions --------------------------------------------------------
+ * kind: 0 = ReduceSum, 1 = ReduceMean.  `axes` are normalised axes of x
+ * (sorted, distinct, >= 0); out has x's shape with the reduced axes removed
+ * (keepdims = 0) or set to 1 (keepdims = 1).  fp32 sums follow numpy's
+ * pairwise order over a contiguous reduced block and its sequential order
+ * over an outer reduced axis, so results are bit-identical to numpy.
+ * replaces: ref_runtime.py:589-598; executor.gd:942-974 (_run_reduce);
+ *           kernels/reduce.glsl:30-61. */
+#define BT_REDUCE_SUM 0
+#define BT_REDUCE_MEAN 1
+int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int n_axes,
+              int keepdims, const bt_tensor* out);
+
+/* ---- softmax -----------------------------------------------------------
+ * out = softmax(x + mask) along `axis` (mask optional, broadcast to x),
+ * in numpy's order: max, exp(x - max), pairwise sum, divide.
+ * replaces: ref_runtime.py:269-273 + :599-600 (and the Add of the attention
+ *           mask that precedes it, :446-447); executor.gd:887-903;
+ *           kernels/softmax.glsl:26-61. */
+int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis,
+               const bt_tensor* out);
+
+/* ---- layer normalisation -----------------------------------------------
+ * out = LN(x [+ skip [+ bias]]) over the axes from `axis` to the last, with
+ * gamma (required) and beta (optional); eps is applied as float32.  skip/bias
+ * NULL gives LayerNormalization, non-NULL gives SkipLayerNormalization.
+ * replaces: ref_runtime.py:276-285 + :601-609; executor.gd:906-939;
+ *           kernels/layernorm.glsl:35-75. */
+int bt_layernorm(const bt_tensor* x, const bt_tensor* skip,
+                 const bt_tensor* bias, const bt_tensor* gamma,
+                 const bt_tensor* beta, int axis, float eps,
+                 const bt_tensor* out);
+
+/* ---- AdaIN1d + Snake (row-fused) ----------------------------------------
+ * For rows r of a [R, T] view (R = batch * channels, T contiguous):
+ *   h      = src0 [+ src1 [+ src2]]          (fp32, left to right)
+ *   if res != NULL: res = h                  (residual written once)
+ *   n      = (h - mean(h)) / sqrt(mean((h - mean)^2) + eps)
+ *   y_k    = gain_k[r] * n + shift_k[r]      for each output k < n_out
+ *   out_k  = y_k + inv_alpha_k[c] * sin(alpha_k[c] * y_k)^2   (snake)
+ *            or y_k when alpha_k == NULL
+ * which is the op chain the packed Kokoro graph runs per AdaIN1d + Snake
+ * (ReduceMean, Sub, Mul, ReduceMean, Add eps, Sqrt, Div, Mul, Add, then Mul,
+ * Sin, Pow 2, Mul, Add), rounded op by op.  Row r is (batch b, channel c)
+ * with b = r / C, c = r % C; gain_k / shift_k are fp32 [B, C] views read at
+ * b * param_stride + c (gain_stride / shift_stride elements between batch
+ * entries, e.g. 2C for the halves of an fc output [B, 2C]); alpha /
+ * inv_alpha are [C] (fp16 or fp32).
+ * Up to three outputs share one normalisation: the graph computes the
+ * instance norm of x once for the three resblocks that read the same x.
+ * replaces: the ReduceMean/Sub/.../Add chains that executor.gd:678-699 and
+ *           :942-974 dispatch one op at a time (ref_runtime.py:446-479,
+ *           :589-598 per op). */
+#define BT_ADAIN_MAX_SRC 3
+#define BT_ADAIN_MAX_OUT 3
+typedef struct bt_adain_args {
+  int64_t rows, cols, channels;          /* R, T, C */
+  int32_t n_src, n_out;
+  const float* src[BT_ADAIN_MAX_SRC];    /* [R, T] fp32, contiguous */
+  float*       res;                      /* [R, T] fp32 or NULL */
+  float        eps;                      /* as float32 */
+  int64_t      gain_stride, shift_stride;/* batch strides of gain / shift */
+  const float* gain[BT_ADAIN_MAX_OUT];   /* [B, C] fp32 views */
+  const float* shift[BT_ADAIN_MAX_OUT];
+  const void*  alpha[BT_ADAIN_MAX_OUT];  /* [C] or NULL (no snake) */
+  const void*  inv_alpha[BT_ADAIN_MAX_OUT];
+  int32_t      alpha_dtype;              /* BT_F16 or BT_F32 */
+  float*       out[BT_ADAIN_MAX_OUT];    /* [R, T] fp32 */
+} bt_adain_args;
+int bt_adain_snake(const bt_adain_args* a);
+
+/* ---- residual mean + LeakyRelu (end of a generator stage) ---------------
+ * out = leaky((((a0 + b0) + (a1 + b1)) + (a2 + b2)) / 3, slope) elementwise
+ * over n fp32 elements: the last residual Add of each of the three resblocks,
+ * the two Adds and the Div by 3 of the resblock mean, and the LeakyRelu that
+ * starts the next stage (or ends the generator), rounded op by op.
+ * replaces: the Add/Add/Div/LeakyRelu dispatches of executor.gd:678-699 at
+ * the end of each generator stage (ref_runtime.py:446-455, :476-479). */
+int bt_resblock_mean_leaky(const float* const* a, const float* const* b,
+                           int64_t n, float divisor, float slope, float* out);
+
+/* ---- host-only helpers (no GPU) ------------------------------------------ */
+/* Broadcast-and-collapse planner used by bt_elementwise: merges adjacent axes
+ * that every operand walks contiguously and drops size-1 axes (the behaviour
+ * of runtime/ops.gd:62-129).  Writes the collapsed rank, shape and the
+ * collapsed strides of the n_ops operands (operand k's strides at
+ * strides_out[k * BT_MAX_RANK + d]).  replaces: ops.gd:45-129. */
+int bt_plan_broadcast(int n_ops, const bt_tensor* ops, const int64_t* out_shape,
+                      int out_rank, int* rank_out, int64_t* shape_out,
+                      int64_t* strides_out);
+/* Evaluates the library's float32 math routines on the host, element by
+ * element, so CPU tests can compare them with numpy.  kind: 0 exp, 1 sin,
+ * 2 cos, 3 sigmoid, 4 pairwise row sum (n values -> out[0]). */
+int bt_host_math(int kind, const float* in, float* out, int64_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BT_OPS_H */
