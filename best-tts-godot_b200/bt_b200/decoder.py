@@ -46,7 +46,7 @@ import torch
 
 from . import _lib
 from ._lib import check, load, make_tensor
-from .runtime import BtRuntime, tensor_desc, NP_TO_TORCH
+from .runtime import as_cuda_device, tensor_desc
 
 EPS = np.float16(1e-5)           # the graph's AdaIN epsilon constant (fp16)
 STYLE_DIM = 128
@@ -320,7 +320,7 @@ class FusedDecoder:
 
     def __init__(self, S, device=None):
         self.S = S
-        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.device = as_cuda_device(device)
         self.lib = load()
         with torch.cuda.device(self.device):
             check(self.lib.bt_init(self.device.index), "bt_init")

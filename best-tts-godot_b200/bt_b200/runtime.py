@@ -55,6 +55,15 @@ _UNARY_NP = {"Sqrt": np.sqrt, "Exp": np.exp, "Sin": np.sin, "Cos": np.cos, "Atan
 COMPARE = {"Greater": "GREATER", "Less": "LESS", "GreaterOrEqual": "GEQ"}
 
 
+def as_cuda_device(device):
+    """torch.device for an ordinal, a torch.device or None (current device)."""
+    if device is None:
+        return torch.device("cuda", torch.cuda.current_device())
+    if isinstance(device, torch.device):
+        return device if device.index is not None else torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cuda", int(device))
+
+
 def np_dtype(t):
     return np.dtype(TORCH_TO_NP[t.dtype])
 
@@ -85,7 +94,7 @@ class BtRuntime:
     def __init__(self, device=None):
         if not torch.cuda.is_available():
             raise RuntimeError("BtRuntime needs a CUDA device (there is no CPU fallback)")
-        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.device = as_cuda_device(device)
         self.lib = load()
         with torch.cuda.device(self.device):
             check(self.lib.bt_init(self.device.index), "bt_init")
@@ -457,25 +466,14 @@ class BtRuntime:
         return out
 
     def dequant_mul(self, q, scale, zero_point, gain):
-        """Mul(DequantizeLinear(q, scale, zero_point), gain) in one pass: the
-        c4 weight path, rounded like the two reference ops
-        (ref_runtime.py:631-636 then :450-451)."""
-        ins = [q, scale, gain] + ([zero_point] if zero_point is not None else [])
-        prog = _lib.BtChain()
-        prog.n_in = len(ins)
-        code = []
-        src = 0
-        if zero_point is not None:
-            code.append((OP["SUB"], 4, 0, 3))    # r4 = q - zp
-            src = 4
-        code.append((OP["MUL"], 4, src, 1))      # r4 = (q - zp) * scale
-        code.append((OP["MUL"], 4, 4, 2))        # r4 = r4 * gain
-        for i, (op, d, a, b) in enumerate(code):
-            prog.instr[i] = _lib.BtChainInstr(op, d, a, b, 0.0)
-        prog.n_instr = len(code)
-        prog.out_reg = 4
+        """Mul(DequantizeLinear(q, scale, zero_point), gain): the c4 weight
+        path, rounded like the two reference ops (ref_runtime.py:631-636
+        then :450-451) -- two library launches."""
+        ins = [q, scale] + ([zero_point] if zero_point is not None else [])
         shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
-        return self.chain(prog, ins, shape)
+        d = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
+        shape2 = np.broadcast_shapes(shape, tuple(gain.shape))
+        return self.elementwise("MUL", [d, self._as_f32(gain)], shape2, np.float32, np.float32)
 
     def adain_snake(self, srcs, gain, shift, eps, alpha=None, inv_alpha=None, res=None, outs=None):
         """Row-fused AdaIN1d (+ Snake) of [B, C, T] float32 tensors (see

@@ -105,21 +105,188 @@ BT_HD float np_expf(float x) {
 }
 
 // ---------------------------------------------------------------------------
+// Double-precision sine / cosine without local memory (the library's own
+// implementation; used where numpy leaves its SIMD path -- it calls the C
+// library for |x| beyond 117435.992 (sine) / 71476.0625 (cosine) -- and for
+// float64 results).  Argument reduction x = q*pi/2 + r:
+//   |x| <= 2^20: Cody-Waite with pi/2 split into a 33-bit, a 33-bit and a
+//     53-bit part (q*hi and q*mid are exact products);
+//   larger |x|: Payne-Hanek -- the 53-bit mantissa times a 160-bit window of
+//     the binary expansion of 2/pi, in 32-bit limbs held in named registers.
+// sin(r), cos(r) on |r| <= pi/4 by their Taylor series to degree 21 / 22.
+// The 2/pi words below are the first 1600 fractional bits of 2/pi, computed
+// from Machin's formula pi = 16 atan(1/5) - 4 atan(1/239) at 520 digits.
+// ---------------------------------------------------------------------------
+#define BT_TWO_OVER_PI_WORDS \
+    0xa2f9836eu, 0x4e441529u, 0xfc2757d1u, 0xf534ddc0u, 0xdb629599u, 0x3c439041u, \
+    0xfe5163abu, 0xdebbc561u, 0xb7246e3au, 0x424dd2e0u, 0x06492eeau, 0x09d1921cu, \
+    0xfe1deb1cu, 0xb129a73eu, 0xe88235f5u, 0x2ebb4484u, 0xe99c7026u, 0xb45f7e41u, \
+    0x3991d639u, 0x835339f4u, 0x9c845f8bu, 0xbdf9283bu, 0x1ff897ffu, 0xde05980fu, \
+    0xef2f118bu, 0x5a0a6d1fu, 0x6d367ecfu, 0x27cb09b7u, 0x4f463f66u, 0x9e5fea2du, \
+    0x7527bac7u, 0xebe5f17bu, 0x3d0739f7u, 0x8a5292eau, 0x6bfb5fb1u, 0x1f8d5d08u, \
+    0x56033046u, 0xfc7b6babu, 0xf0cfbc20u, 0x9af4361du, 0xa9e39161u, 0x5ee61b08u, \
+    0x6599855fu, 0x14a06840u, 0x8dffd880u, 0x4d732731u, 0x06061556u, 0xca73a8c9u, \
+    0x60e27bc0u, 0x8c6b47c4u
+constexpr int kTwoOverPiWords = 50;
+#if defined(__CUDACC__)
+static __constant__ uint32_t kTwoOverPiDev[kTwoOverPiWords] = {BT_TWO_OVER_PI_WORDS};
+#endif
+static const uint32_t kTwoOverPiHost[kTwoOverPiWords] = {BT_TWO_OVER_PI_WORDS};
+
+BT_HD uint32_t two_over_pi_word(int i) {
+  if (i < 0 || i >= kTwoOverPiWords) return 0u;
+#if defined(__CUDA_ARCH__)
+  return kTwoOverPiDev[i];
+#else
+  return kTwoOverPiHost[i];
+#endif
+}
+
+#if defined(__CUDA_ARCH__)
+#define BT_DADD(a, b) __dadd_rn((a), (b))
+#define BT_DMUL(a, b) __dmul_rn((a), (b))
+#define BT_DFMA(a, b, c) __fma_rn((a), (b), (c))
+#else
+#define BT_DADD(a, b) ((a) + (b))
+#define BT_DMUL(a, b) ((a) * (b))
+#define BT_DFMA(a, b, c) fma((a), (b), (c))
+#endif
+
+BT_HD uint64_t d_bits(double d) {
+#if defined(__CUDA_ARCH__)
+  return (uint64_t)__double_as_longlong(d);
+#else
+  union { uint64_t u; double d; } v; v.d = d; return v.u;
+#endif
+}
+
+// 32-bit limb i of a 224-bit number held in c0..c6.
+BT_HD uint64_t limb7(int i, uint64_t c0, uint64_t c1, uint64_t c2, uint64_t c3, uint64_t c4, uint64_t c5,
+                     uint64_t c6) {
+  switch (i) {
+    case 0: return c0; case 1: return c1; case 2: return c2; case 3: return c3;
+    case 4: return c4; case 5: return c5; case 6: return c6;
+  }
+  return 0;
+}
+
+// Bits [p, p + 64) of the number held in c0..c6.
+BT_HD uint64_t bits64_at(int p, uint64_t c0, uint64_t c1, uint64_t c2, uint64_t c3, uint64_t c4, uint64_t c5,
+                         uint64_t c6) {
+  const int i = p >> 5, off = p & 31;
+  uint64_t v = limb7(i, c0, c1, c2, c3, c4, c5, c6) >> off;
+  v |= limb7(i + 1, c0, c1, c2, c3, c4, c5, c6) << (32 - off);
+  if (off > 0) v |= limb7(i + 2, c0, c1, c2, c3, c4, c5, c6) << (64 - off);
+  return v;
+}
+
+// |x| = q*pi/2 + r with |r| <= pi/4 (approximately), for finite |x| > 2^20.
+BT_HD double reduce_pio2_large(double ax, int* quad) {
+  const uint64_t b = d_bits(ax);
+  const int E = (int)((b >> 52) & 0x7ff) - 1023;
+  const uint64_t m = (b & ((1ull << 52) - 1)) | (1ull << 52);
+  const int e = E - 52;                      // ax = m * 2^e
+  const int j0 = (e - 1 > 1) ? e - 1 : 1;    // first bit of 2/pi that matters mod 4
+  const int i0 = j0 - 1, wi = i0 >> 5, bo = i0 & 31;
+  uint64_t w[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    uint32_t hi = two_over_pi_word(wi + k), lo = two_over_pi_word(wi + k + 1);
+    w[k] = bo ? (uint64_t)(uint32_t)((hi << bo) | (lo >> (32 - bo))) : (uint64_t)hi;
+  }
+  const uint64_t M = 0xffffffffull, ml = m & M, mh = m >> 32;
+  const uint64_t a0 = ml * w[4], a1 = ml * w[3], a2 = ml * w[2], a3 = ml * w[1], a4 = ml * w[0];
+  const uint64_t b1 = mh * w[4], b2 = mh * w[3], b3 = mh * w[2], b4 = mh * w[1], b5 = mh * w[0];
+  uint64_t c0 = a0 & M;
+  uint64_t c1 = (a0 >> 32) + (a1 & M) + (b1 & M);
+  uint64_t c2 = (a1 >> 32) + (a2 & M) + (b1 >> 32) + (b2 & M);
+  uint64_t c3 = (a2 >> 32) + (a3 & M) + (b2 >> 32) + (b3 & M);
+  uint64_t c4 = (a3 >> 32) + (a4 & M) + (b3 >> 32) + (b4 & M);
+  uint64_t c5 = (a4 >> 32) + (b4 >> 32) + (b5 & M);
+  uint64_t c6 = (b5 >> 32);
+  c1 += c0 >> 32; c0 &= M;
+  c2 += c1 >> 32; c1 &= M;
+  c3 += c2 >> 32; c2 &= M;
+  c4 += c3 >> 32; c3 &= M;
+  c5 += c4 >> 32; c4 &= M;
+  c6 += c5 >> 32; c5 &= M;
+  const int sh = j0 + 159 - e;               // x*2/pi = P * 2^-sh (mod 4)
+  const uint64_t frac = bits64_at(sh - 64, c0, c1, c2, c3, c4, c5, c6);
+  int q = (int)(bits64_at(sh, c0, c1, c2, c3, c4, c5, c6) & 3);
+  q += (int)(frac >> 63);                    // round to the nearest quadrant
+  *quad = q & 3;
+  const double f = (double)(int64_t)frac * 5.421010862427522e-20;   // 2^-64
+  return BT_DMUL(f, 0x1.921fb54442d18p+0);
+}
+
+// Taylor coefficients (-1)^k / (2k+1)! and (-1)^k / (2k)!, correctly rounded.
+BT_HD double sin_taylor(double r) {
+  const double r2 = BT_DMUL(r, r);
+  double p = 0x1.71b8ef6dcf572p-66;          // +1/21!
+  p = BT_DFMA(p, r2, -0x1.2f49b46814157p-57);  // -1/19!
+  p = BT_DFMA(p, r2, 0x1.952c77030ad4ap-49);   // +1/17!
+  p = BT_DFMA(p, r2, -0x1.ae7f3e733b81fp-41);  // -1/15!
+  p = BT_DFMA(p, r2, 0x1.6124613a86d09p-33);   // +1/13!
+  p = BT_DFMA(p, r2, -0x1.ae64567f544e4p-26);  // -1/11!
+  p = BT_DFMA(p, r2, 0x1.71de3a556c734p-19);   // +1/9!
+  p = BT_DFMA(p, r2, -0x1.a01a01a01a01ap-13);  // -1/7!
+  p = BT_DFMA(p, r2, 0x1.1111111111111p-7);    // +1/5!
+  p = BT_DFMA(p, r2, -0x1.5555555555555p-3);   // -1/3!
+  return BT_DFMA(BT_DMUL(p, r2), r, r);
+}
+BT_HD double cos_taylor(double r) {
+  const double r2 = BT_DMUL(r, r);
+  double p = -0x1.0ce396db7f853p-70;         // -1/22!
+  p = BT_DFMA(p, r2, 0x1.e542ba4020225p-62);   // +1/20!
+  p = BT_DFMA(p, r2, -0x1.6827863b97d97p-53);  // -1/18!
+  p = BT_DFMA(p, r2, 0x1.ae7f3e733b81fp-45);   // +1/16!
+  p = BT_DFMA(p, r2, -0x1.93974a8c07c9dp-37);  // -1/14!
+  p = BT_DFMA(p, r2, 0x1.1eed8eff8d898p-29);   // +1/12!
+  p = BT_DFMA(p, r2, -0x1.27e4fb7789f5cp-22);  // -1/10!
+  p = BT_DFMA(p, r2, 0x1.a01a01a01a01ap-16);   // +1/8!
+  p = BT_DFMA(p, r2, -0x1.6c16c16c16c17p-10);  // -1/6!
+  p = BT_DFMA(p, r2, 0x1.5555555555555p-5);    // +1/4!
+  p = BT_DFMA(p, r2, -0.5);                    // -1/2!
+  return BT_DFMA(p, r2, 1.0);
+}
+
+BT_HD double bt_sincos_d(double x, bool cosine) {
+  if (x != x) return x;
+  const double ax = fabs(x);
+  if (ax == INFINITY) return ax - ax;  // NaN
+  int q;
+  double r;
+  if (ax <= 1048576.0) {
+    const double t = BT_DMUL(ax, 0x1.45f306dc9c883p-1);
+    const double qd = rint(t);
+    r = BT_DFMA(-qd, 0x1.921fb54400000p+0, ax);
+    r = BT_DFMA(-qd, 0x1.0b4611a600000p-34, r);
+    r = BT_DFMA(-qd, 0x1.3198a2e037073p-69, r);
+    q = (int)((int64_t)qd & 3);
+  } else {
+    r = reduce_pio2_large(ax, &q);
+  }
+  if (cosine) q += 1;
+  double v = (q & 1) ? cos_taylor(r) : sin_taylor(r);
+  if (q & 2) v = -v;
+  if (!cosine && x < 0) v = -v;
+  if (!cosine && x == 0) v = x;   // sin(+-0) = +-0
+  return v;
+}
+
+// ---------------------------------------------------------------------------
 // sin / cos: numpy's float32 SIMD algorithm.  q = round(x * 2/pi) (computed
 // as one fused multiply-add with the 1.5*2^23 rounding constant), a
 // three-part Cody-Waite reduction r = x - q*pi/2, then the sine polynomial
 // (odd, degree 9) or the cosine polynomial (even, degree 8) on r chosen by
 // the quadrant, negated in quadrants 2 and 3.  Beyond |x| = 117435.992
-// (sine) or 71476.0625 (cosine) numpy falls back to the C library, which
-// this code replaces with a double-precision evaluation rounded to float.
+// (sine) or 71476.0625 (cosine) numpy falls back to the C library; there
+// bt_sincos_d (double precision, rounded to float) stands in for it.
 // ---------------------------------------------------------------------------
 BT_HD float np_sincosf(float x, bool cosine) {
   if (is_nan(x)) return qnan();
   const float lim = cosine ? 71476.0625f : 117435.992f;
-  if (!(fabsf(x) <= lim)) {
-    double d = (double)x;
-    return (float)(cosine ? cos(d) : sin(d));
-  }
+  if (!(fabsf(x) <= lim)) return (float)bt_sincos_d((double)x, cosine);
   const float kTwoOverPi = 0x1.45f306p-1f;
   const float kMagic = 12582912.0f;
   float q = BT_SUB(BT_FMA(x, kTwoOverPi, kMagic), kMagic);

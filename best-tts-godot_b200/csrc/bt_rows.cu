@@ -405,34 +405,46 @@ struct AdainArgs {
 
 __global__ void adain_snake_kernel(AdainArgs A) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const bt_adain_args& a = A.p;
+  // Scalars and per-output pointers are read from the parameter block with
+  // compile-time indices (no reference to the parameter block is taken).
   const int n = A.n;
+  const int64_t rows = A.p.rows, channels = A.p.channels;
+  const int n_src = A.p.n_src, n_out = A.p.n_out, adt = A.p.alpha_dtype;
+  const int64_t gstride = A.p.gain_stride, sstride = A.p.shift_stride;
+  const float eps = A.p.eps;
+  const float* src0 = A.p.src[0];
+  const float* src1 = A.p.src[1];
+  const float* src2 = A.p.src[2];
+  float* resp = A.p.res;
   PwPlan P = plan_at(plan_area(smem, n), A.depth);
   pw_build(P, n);
-  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const int64_t base = row * (int64_t)n;
-    const float* g0 = a.src[0] + base;
+    const float* g0 = src0 + base;
     float* s = row_buffer(smem, g0);
-    stage_row(s, g0, a.n_src > 1 ? a.src[1] + base : nullptr, a.n_src > 2 ? a.src[2] + base : nullptr, n,
-              a.res ? a.res + base : nullptr);
+    stage_row(s, g0, n_src > 1 ? src1 + base : nullptr, n_src > 2 ? src2 + base : nullptr, n,
+              resp ? resp + base : nullptr);
     __syncthreads();
     // ReduceMean -> Sub -> Mul(d, d) -> ReduceMean -> Add eps -> Sqrt
     const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum<false>(s, P)), n);
     for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_SUB(s[i], mu);
     __syncthreads();
     const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum<true>(s, P)), n);
-    const float sd = BT_SQRT(BT_ADD(var, a.eps));
-    const int64_t c = row % a.channels, b = row / a.channels;
+    const float sd = BT_SQRT(BT_ADD(var, eps));
+    const int64_t c = row % channels, b = row / channels;
     const RowSplit sp = row_split(g0, n);
-    for (int k = 0; k < a.n_out; ++k) {
-      const float gain = a.gain[k][b * a.gain_stride + c], shift = a.shift[k][b * a.shift_stride + c];
-      const bool snake = a.alpha[k] != nullptr;
+#pragma unroll
+    for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
+      if (k >= n_out) break;
+      const float gain = A.p.gain[k][b * gstride + c], shift = A.p.shift[k][b * sstride + c];
+      const void* alpha_k = A.p.alpha[k];
+      const bool snake = alpha_k != nullptr;
       float al = 0.f, ial = 0.f;
       if (snake) {
-        al = ldf(a.alpha[k], a.alpha_dtype, c);
-        ial = ldf(a.inv_alpha[k], a.alpha_dtype, c);
+        al = ldf(alpha_k, adt, c);
+        ial = ldf(A.p.inv_alpha[k], adt, c);
       }
-      float* o = a.out[k] + base;
+      float* o = A.p.out[k] + base;
       // Div -> Mul(1+gamma) -> Add(beta) [-> Mul(alpha) -> Sin -> Pow 2 -> Mul(1/alpha) -> Add]
       auto f = [&](float d) -> float {
         float y = BT_ADD(BT_MUL(gain, BT_DIV(d, sd)), shift);

@@ -150,3 +150,16 @@ def test_host_pairwise_sum_is_numpy_exact(lib, n):
     got = _host_math(4, x)[0]
     want = np.float32(x.sum())
     assert got.view(np.uint32) == want.view(np.uint32)
+
+
+def test_fused_chain_validates_then_reports_withdrawn(lib):
+    """The register-program entry point validates its arguments and then
+    reports that its kernel is withdrawn (it faulted on the B200)."""
+    prog = _lib.BtChain()
+    prog.n_in = 0
+    x = _lib.make_tensor(0x1000, np.float32, (4,))
+    assert lib.bt_fused_chain(ctypes.byref(prog), (_lib.BtTensor * 1)(x), ctypes.byref(x)) == -1
+    prog.n_in, prog.n_instr, prog.out_reg = 1, 1, 1
+    prog.instr[0] = _lib.BtChainInstr(0, 1, 0, 0, 0.0)
+    assert lib.bt_fused_chain(ctypes.byref(prog), (_lib.BtTensor * 1)(x), ctypes.byref(x)) == -5
+    assert b"withdrawn" in lib.bt_last_error()
