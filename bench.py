@@ -301,7 +301,7 @@ def per_op(rt, torch, peak):
                                                                      alpha=0.2), nb, flush, 5, torch)
         sweep[nm] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     gl = torch.rand(768, device="cuda")
-    Al = A.reshape(-1, 768)[: (n // 768)]
+    Al = A.reshape(-1)[: (n // 768) * 768].reshape(-1, 768)
     ms, gbs = measure_op(lambda: rt.layernorm(Al, None, None, gl, None, -1, 1e-5), 2 * Al.numel() * 4 + 3072,
                          flush, 5, torch)
     sweep["layernorm_768"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
@@ -445,7 +445,7 @@ def run_b200(args):
                 "vs_baseline": None, "dtype": "f32", "data": DATA, "config": config(args, n),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk, "stream_algorithmic_bytes_per_step": stream_bytes,
-                "stream_GBps": round(stream_bytes * args.steps / elapsed / n / 1e9 * n, 1),
+                "stream_GBps_per_gpu": round(stream_bytes * args.steps / elapsed / 1e9, 1),
                 "stream_frac_of_measured": round(stream_bytes / (elapsed / args.steps) / 1e9 / peak, 4)}
         line.update(extra)
         print(json.dumps(line), flush=True)
