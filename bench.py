@@ -455,6 +455,30 @@ def run_b200(args):
     return 0
 
 
+def run_profile_adain(args):
+    """One kind of stage-2 bt_adain_snake launch (two sources + residual +
+    snake output, the most common launch of the stream) on its own, for ncu:
+    batch x 128 rows of 24001 values, every array larger than L2."""
+    import torch
+    from bt_b200.runtime import BtRuntime
+    torch.cuda.set_device(0)
+    rt = BtRuntime(0)
+    B, C, T = args.batch, 128, args.t0 * 60 + 1
+    g = torch.Generator(device="cuda").manual_seed(5)
+    srcs = [torch.randn((B, C, T), device="cuda", generator=g) for _ in range(2)]
+    res = torch.empty((B, C, T), device="cuda")
+    out = [torch.empty((B, C, T), device="cuda")]
+    fc = torch.randn((B, 2 * C), device="cuda", generator=g)
+    alpha = (torch.rand(C, device="cuda", generator=g) + 0.5).half()
+    inv = (1.0 / alpha.float()).half()
+    for _ in range(args.warmup + args.steps):
+        rt.adain_snake(srcs, fc[:, :C], fc[:, C:], 1e-5, alpha, inv, res=res, outs=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "adain_snake stage 2, 2 sources + residual + snake", "rows": B * C, "cols": T,
+                      "launches": args.warmup + args.steps}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,7 +490,11 @@ def main():
     ap.add_argument("--cpu-procs", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-op", action="store_true")
+    ap.add_argument("--profile-adain", action="store_true",
+                    help="run only stage-2 bt_adain_snake launches (for ncu)")
     args = ap.parse_args()
+    if args.profile_adain:
+        return run_profile_adain(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

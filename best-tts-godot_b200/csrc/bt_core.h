@@ -250,7 +250,13 @@ BT_HD double cos_taylor(double r) {
   return BT_DFMA(p, r2, 1.0);
 }
 
-BT_HD double bt_sincos_d(double x, bool cosine) {
+#if defined(__CUDACC__)
+#define BT_COLD static __host__ __device__ __noinline__
+#else
+#define BT_COLD static inline
+#endif
+
+BT_COLD double bt_sincos_d(double x, bool cosine) {
   if (x != x) return x;
   const double ax = fabs(x);
   if (ax == INFINITY) return ax - ax;  // NaN

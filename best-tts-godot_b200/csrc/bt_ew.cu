@@ -283,47 +283,65 @@ __global__ void __launch_bounds__(256) ew_nd_kernel(EwArgs a) {
 // Flat (rank 1) float32 path: every input is a scalar or a unit-stride run,
 // the output is a unit-stride run.  VEC = 4 when every unit-stride operand
 // starts on a 4-element boundary of its own type.
+// Loads VEC consecutive elements of operand o starting at element `base`
+// (VEC = 4: one 128-bit fp32, 64-bit fp16 or 32-bit int8 load).
+template <int VEC>
+__device__ __forceinline__ void ld_vec(const Operand& o, int64_t base, float* x) {
+  if (o.st[0] == 0) {
+    const float s = ld1<float>(o.p, o.dt, 0);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) x[j] = s;
+  } else if (VEC == 4 && o.dt == BT_F32) {
+    const float4 f = __ldcs((const float4*)((const float*)o.p + base));
+    x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
+  } else if (VEC == 4 && o.dt == BT_F16) {
+    uint2 u = __ldcs((const uint2*)((const __half*)o.p + base));
+    __half2 h0 = *reinterpret_cast<__half2*>(&u.x), h1 = *reinterpret_cast<__half2*>(&u.y);
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    x[0] = f0.x; x[1] = f0.y; x[2] = f1.x; x[3] = f1.y;
+  } else if (VEC == 4 && o.dt == BT_I8) {
+    const int w = __ldcs((const int*)((const signed char*)o.p + base));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = (float)(signed char)(w >> (8 * j));
+  } else {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) x[j] = ld1<float>(o.p, o.dt, base + j);
+  }
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(256) ew_flat_kernel(EwArgs a) {
   const int64_t nv = a.n / VEC;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += stride) {
-    const int64_t base = v * VEC;
-    float x[3][VEC];
+  // U vectors per thread per iteration, all loads issued before the math.
+  constexpr int U = 2;
+  for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
+    float x[U][3][VEC];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      if (k >= a.n_in) break;
-      const Operand& o = a.in[k];
-      if (o.st[0] == 0) {
-        float s = ld1<float>(o.p, o.dt, 0);
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v < nv) {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) x[k][j] = s;
-      } else if (VEC == 4 && o.dt == BT_F32) {
-        float4 f = __ldcs((const float4*)((const float*)o.p + base));
-        x[k][0] = f.x; x[k][1] = f.y; x[k][2] = f.z; x[k][3] = f.w;
-      } else if (VEC == 4 && o.dt == BT_F16) {
-        uint2 u = __ldcs((const uint2*)((const __half*)o.p + base));
-        __half2 h0 = *reinterpret_cast<__half2*>(&u.x), h1 = *reinterpret_cast<__half2*>(&u.y);
-        float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-        x[k][0] = f0.x; x[k][1] = f0.y; x[k][2] = f1.x; x[k][3] = f1.y;
-      } else if (VEC == 4 && o.dt == BT_I8) {
-        int w = __ldcs((const int*)((const signed char*)o.p + base));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x[k][j] = (float)(signed char)(w >> (8 * j));
-      } else {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) x[k][j] = ld1<float>(o.p, o.dt, base + j);
+        for (int k = 0; k < 3; ++k)
+          if (k < a.n_in) ld_vec<VEC>(a.in[k], v * VEC, x[u][k]);
       }
     }
-    float r[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j)
-      r[j] = apply_f32(a.op, x[0][j], a.n_in > 1 ? x[1][j] : 0.f, a.n_in > 2 ? x[2][j] : 0.f, a.alpha, a.n_in);
-    if (VEC == 4 && a.odt == BT_F32) {
-      __stcs((float4*)((float*)a.out + base), make_float4(r[0], r[1], r[2], r[3]));
-    } else {
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v >= nv) break;
+      const int64_t base = v * VEC;
+      float r[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, base + j, r[j]);
+      for (int j = 0; j < VEC; ++j)
+        r[j] = apply_f32(a.op, x[u][0][j], a.n_in > 1 ? x[u][1][j] : 0.f, a.n_in > 2 ? x[u][2][j] : 0.f, a.alpha,
+                         a.n_in);
+      if (VEC == 4 && a.odt == BT_F32) {
+        __stcs((float4*)((float*)a.out + base), make_float4(r[0], r[1], r[2], r[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, base + j, r[j]);
+      }
     }
   }
   // tail

@@ -45,4 +45,9 @@ struct BcastPlan {
 int plan_broadcast(int n_ops, const bt_tensor* const* ops,
                    const int64_t* out_shape, int out_rank, BcastPlan* p);
 
+// AdaIN1d + Snake with rows split across a thread-block cluster (bt_adain.cu).
+// Returns BT_EUNSUPPORTED, without setting an error, for requests it does
+// not cover; bt_adain_snake then uses the one-CTA-per-row kernel.
+int adain_v3(const bt_adain_args* p);
+
 }  // namespace bt

@@ -87,57 +87,91 @@ __device__ void pw_build(PwPlan& P, int n) {
   __syncthreads();
 }
 
+// Element transforms applied while summing: the value itself, or its
+// squared deviation from a mean (Sub then Mul, each rounded).
+struct PwIdentity {
+  __device__ __forceinline__ float operator()(float v) const { return v; }
+};
+struct PwSquaredDev {
+  float mu;
+  __device__ __forceinline__ float operator()(float v) const {
+    const float d = BT_SUB(v, mu);
+    return BT_MUL(d, d);
+  }
+};
+
 // numpy's pairwise sum of f(s[0..n)) with the plan in P (whole CTA; every
-// thread receives the result).  SQUARE selects f(v) = v*v.
-template <bool SQUARE>
-__device__ float pw_sum(const float* s, PwPlan& P) {
-  const int lane8 = threadIdx.x & 7;
-  const int grp = threadIdx.x >> 3, ngrp = blockDim.x >> 3;
-  const unsigned gmask = 0xFFu << (threadIdx.x & 24);
+// thread receives the result).  Two lanes per leaf, each holding four of
+// numpy's eight accumulators (lane h owns r[4h..4h+3]); `aligned` means s is
+// 16-byte aligned, so every leaf (leaf offsets are multiples of 8) can be read
+// with 128-bit shared loads.  The inner nodes are combined by one warp, level
+// by level.
+template <class F>
+__device__ float pw_sum(const float* s, PwPlan& P, F f, bool aligned) {
+  const int h = threadIdx.x & 1;
+  const int grp = threadIdx.x >> 1, ngrp = blockDim.x >> 1;
+  const unsigned pmask = 3u << (threadIdx.x & 30);
   const int nl = *P.n_leaf;
   for (int L = grp; L < nl; L += ngrp) {
     const int off = P.leaf_off[L], len = P.leaf_len[L];
-    float res;
+    float res = 0.0f;
     if (len < 8) {
-      res = 0.0f;
-      if (lane8 == 0)
-        for (int i = 0; i < len; ++i) {
-          float v = s[off + i];
-          res = BT_ADD(res, SQUARE ? BT_MUL(v, v) : v);
-        }
+      if (h == 0)
+        for (int i = 0; i < len; ++i) res = BT_ADD(res, f(s[off + i]));
     } else {
-      float v = s[off + lane8];
-      float r = SQUARE ? BT_MUL(v, v) : v;
-      const int full = len - (len & 7);
-      for (int i = 8; i < full; i += 8) {
-        v = s[off + i + lane8];
-        r = BT_ADD(r, SQUARE ? BT_MUL(v, v) : v);
+      const float* q = s + off + 4 * h;
+      float r0, r1, r2, r3;
+      if (aligned) {
+        const float4 v = *(const float4*)q;
+        r0 = f(v.x); r1 = f(v.y); r2 = f(v.z); r3 = f(v.w);
+      } else {
+        r0 = f(q[0]); r1 = f(q[1]); r2 = f(q[2]); r3 = f(q[3]);
       }
-      // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); float addition commutes, so
-      // xor partners reproduce numpy's brackets exactly.
-      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 1));
-      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 2));
-      r = BT_ADD(r, __shfl_xor_sync(gmask, r, 4));
-      res = r;
-      if (lane8 == 0)
-        for (int i = full; i < len; ++i) {
-          v = s[off + i];
-          res = BT_ADD(res, SQUARE ? BT_MUL(v, v) : v);
+      const int full = len & ~7;
+      for (int i = 8; i < full; i += 8) {
+        if (aligned) {
+          const float4 v = *(const float4*)(q + i);
+          r0 = BT_ADD(r0, f(v.x)); r1 = BT_ADD(r1, f(v.y)); r2 = BT_ADD(r2, f(v.z)); r3 = BT_ADD(r3, f(v.w));
+        } else {
+          r0 = BT_ADD(r0, f(q[i])); r1 = BT_ADD(r1, f(q[i + 1]));
+          r2 = BT_ADD(r2, f(q[i + 2])); r3 = BT_ADD(r3, f(q[i + 3]));
         }
+      }
+      // lane 0: (r0+r1)+(r2+r3), lane 1: (r4+r5)+(r6+r7); their sum is numpy's
+      // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) (float addition commutes).
+      float t = BT_ADD(BT_ADD(r0, r1), BT_ADD(r2, r3));
+      t = BT_ADD(t, __shfl_xor_sync(pmask, t, 1));
+      res = t;
+      if (h == 0)
+        for (int i = full; i < len; ++i) res = BT_ADD(res, f(s[off + i]));
     }
-    if (lane8 == 0) P.hsum[P.leaf_id[L]] = res;
+    if (h == 0) P.hsum[P.leaf_id[L]] = res;
   }
   __syncthreads();
-  for (int k = P.depth - 1; k >= 0; --k) {
-    for (int j = threadIdx.x; j < (1 << k); j += blockDim.x) {
-      const int h = (1 << k) + j;
-      if (P.kind[h] == 2) P.hsum[h] = BT_ADD(P.hsum[2 * h], P.hsum[2 * h + 1]);
+  if (threadIdx.x < 32) {
+    for (int k = P.depth - 1; k >= 0; --k) {
+      for (int j = threadIdx.x; j < (1 << k); j += 32) {
+        const int hh = (1 << k) + j;
+        if (P.kind[hh] == 2) P.hsum[hh] = BT_ADD(P.hsum[2 * hh], P.hsum[2 * hh + 1]);
+      }
+      __syncwarp();
     }
-    __syncthreads();
   }
+  __syncthreads();
   const float total = P.hsum[1];
   __syncthreads();  // P may be reused by the caller's next sum
   return total;
+}
+
+// Correctly rounded a / b for a divisor shared by many elements: with
+// rb = RN64(1 / b) computed once, RN32(RN64(a * rb)) == RN32(a / b) for all
+// float a, b.  (A quotient of two floats that is not a float lies at least
+// 2^-50 away (relative) from every float rounding midpoint and is never on
+// one; the double-precision product errs by at most 2^-52, so it rounds to
+// the same float.  Infinities, zeros and NaNs follow IEEE division.)
+__device__ __forceinline__ double recip_d(float b) { return __ddiv_rn(1.0, (double)b); }
+__device__ __forceinline__ float div_by(float a, double rb) {
+  return __double2float_rn(__dmul_rn((double)a, rb));
 }
 
 // np.max-style block maximum (NaN propagates).
@@ -264,7 +298,7 @@ __global__ void reduce_rows_kernel(ReduceRowsArgs a) {
       for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = __half2float(g[i]);
     }
     __syncthreads();
-    const float sum = BT_ADD(0.0f, pw_sum<false>(s, P));
+    const float sum = BT_ADD(0.0f, pw_sum(s, P, PwIdentity(), ((uintptr_t)s & 15) == 0));
     if (threadIdx.x == 0) a.out[row] = a.mean ? np_mean_from_sum(sum, n) : sum;
   }
 }
@@ -332,20 +366,21 @@ __global__ void softmax_rows_kernel(SoftmaxArgs a) {
     const float m = block_max(s, n, red);
     for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = np_expf(BT_SUB(s[i], m));
     __syncthreads();
-    const float denom = BT_ADD(0.0f, pw_sum<false>(s, P));
+    const float denom = BT_ADD(0.0f, pw_sum(s, P, PwIdentity(), ((uintptr_t)s & 15) == 0));
+    const double rd = recip_d(denom);
     float* o = a.out + row * (int64_t)n;
     const RowSplit sp = row_split(o, n);
     const bool vec = phase4(o) == phase4(g);
     if (vec) {
-      for (int i = threadIdx.x; i < sp.head; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+      for (int i = threadIdx.x; i < sp.head; i += blockDim.x) o[i] = div_by(s[i], rd);
       for (int q = threadIdx.x; q < sp.nvec; q += blockDim.x) {
         const int i = sp.head + 4 * q;
         float4 v = *(const float4*)(s + i);
-        __stcs((float4*)(o + i), make_float4(BT_DIV(v.x, denom), BT_DIV(v.y, denom), BT_DIV(v.z, denom), BT_DIV(v.w, denom)));
+        __stcs((float4*)(o + i), make_float4(div_by(v.x, rd), div_by(v.y, rd), div_by(v.z, rd), div_by(v.w, rd)));
       }
-      for (int i = sp.head + 4 * sp.nvec + threadIdx.x; i < n; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+      for (int i = sp.head + 4 * sp.nvec + threadIdx.x; i < n; i += blockDim.x) o[i] = div_by(s[i], rd);
     } else {
-      for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = BT_DIV(s[i], denom);
+      for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = div_by(s[i], rd);
     }
     __syncthreads();
   }
@@ -382,14 +417,14 @@ __global__ void layernorm_rows_kernel(LayerNormArgs a) {
       for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_ADD(s[i], a.bias[i]);
     }
     __syncthreads();
-    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum<false>(s, P)), n);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_SUB(s[i], mu);
-    __syncthreads();
-    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum<true>(s, P)), n);
+    const bool al = ((uintptr_t)s & 15) == 0;
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum(s, P, PwIdentity(), al)), n);
+    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum(s, P, PwSquaredDev{mu}, al)), n);
     const float sd = BT_SQRT(BT_ADD(var, a.eps));
+    const double rsd = recip_d(sd);
     float* o = a.out + row * (int64_t)n;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      float y = BT_MUL(BT_DIV(s[i], sd), ldf(a.gamma, a.gdt, i));
+      float y = BT_MUL(div_by(BT_SUB(s[i], mu), rsd), ldf(a.gamma, a.gdt, i));
       if (a.beta) y = BT_ADD(y, ldf(a.beta, a.bdt, i));
       o[i] = y;
     }
@@ -426,11 +461,11 @@ __global__ void adain_snake_kernel(AdainArgs A) {
               resp ? resp + base : nullptr);
     __syncthreads();
     // ReduceMean -> Sub -> Mul(d, d) -> ReduceMean -> Add eps -> Sqrt
-    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum<false>(s, P)), n);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s[i] = BT_SUB(s[i], mu);
-    __syncthreads();
-    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum<true>(s, P)), n);
+    const bool al = ((uintptr_t)s & 15) == 0;
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, pw_sum(s, P, PwIdentity(), al)), n);
+    const float var = np_mean_from_sum(BT_ADD(0.0f, pw_sum(s, P, PwSquaredDev{mu}, al)), n);
     const float sd = BT_SQRT(BT_ADD(var, eps));
+    const double rsd = recip_d(sd);
     const int64_t c = row % channels, b = row / channels;
     const RowSplit sp = row_split(g0, n);
 #pragma unroll
@@ -445,9 +480,9 @@ __global__ void adain_snake_kernel(AdainArgs A) {
         ial = ldf(A.p.inv_alpha[k], adt, c);
       }
       float* o = A.p.out[k] + base;
-      // Div -> Mul(1+gamma) -> Add(beta) [-> Mul(alpha) -> Sin -> Pow 2 -> Mul(1/alpha) -> Add]
-      auto f = [&](float d) -> float {
-        float y = BT_ADD(BT_MUL(gain, BT_DIV(d, sd)), shift);
+      // Sub -> Div -> Mul(1+gamma) -> Add(beta) [-> Mul(alpha) -> Sin -> Pow 2 -> Mul(1/alpha) -> Add]
+      auto f = [&](float v) -> float {
+        float y = BT_ADD(BT_MUL(gain, div_by(BT_SUB(v, mu), rsd)), shift);
         if (!snake) return y;
         const float t = np_sinf(BT_MUL(al, y));
         return BT_ADD(y, BT_MUL(ial, BT_MUL(t, t)));
@@ -472,14 +507,15 @@ struct MeanLeakyArgs {
   const float* a[3];
   const float* b[3];
   int64_t n;
-  float divisor, slope;
+  double rdiv;    // RN64(1 / divisor)
+  float slope;
   float* out;
 };
 
 __device__ __forceinline__ float mean_leaky(float a0, float b0, float a1, float b1, float a2, float b2,
-                                            float div, float slope) {
+                                            double rdiv, float slope) {
   float v = BT_ADD(BT_ADD(BT_ADD(a0, b0), BT_ADD(a1, b1)), BT_ADD(a2, b2));
-  v = BT_DIV(v, div);
+  v = div_by(v, rdiv);
   return v < 0.0f ? BT_MUL(v, slope) : v;
 }
 
@@ -493,20 +529,20 @@ __global__ void __launch_bounds__(256) mean_leaky_kernel(MeanLeakyArgs m) {
     x[2] = __ldcs((const float4*)(m.a[1] + i)); x[3] = __ldcs((const float4*)(m.b[1] + i));
     x[4] = __ldcs((const float4*)(m.a[2] + i)); x[5] = __ldcs((const float4*)(m.b[2] + i));
     float4 r;
-    r.x = mean_leaky(x[0].x, x[1].x, x[2].x, x[3].x, x[4].x, x[5].x, m.divisor, m.slope);
-    r.y = mean_leaky(x[0].y, x[1].y, x[2].y, x[3].y, x[4].y, x[5].y, m.divisor, m.slope);
-    r.z = mean_leaky(x[0].z, x[1].z, x[2].z, x[3].z, x[4].z, x[5].z, m.divisor, m.slope);
-    r.w = mean_leaky(x[0].w, x[1].w, x[2].w, x[3].w, x[4].w, x[5].w, m.divisor, m.slope);
+    r.x = mean_leaky(x[0].x, x[1].x, x[2].x, x[3].x, x[4].x, x[5].x, m.rdiv, m.slope);
+    r.y = mean_leaky(x[0].y, x[1].y, x[2].y, x[3].y, x[4].y, x[5].y, m.rdiv, m.slope);
+    r.z = mean_leaky(x[0].z, x[1].z, x[2].z, x[3].z, x[4].z, x[5].z, m.rdiv, m.slope);
+    r.w = mean_leaky(x[0].w, x[1].w, x[2].w, x[3].w, x[4].w, x[5].w, m.rdiv, m.slope);
     __stcs((float4*)(m.out + i), r);
   }
   for (int64_t i = nv * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m.n; i += stride)
-    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.divisor, m.slope);
+    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.rdiv, m.slope);
 }
 
 __global__ void mean_leaky_scalar_kernel(MeanLeakyArgs m) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m.n; i += stride)
-    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.divisor, m.slope);
+    m.out[i] = mean_leaky(m.a[0][i], m.b[0][i], m.a[1][i], m.b[1][i], m.a[2][i], m.b[2][i], m.rdiv, m.slope);
 }
 
 // ---- launch helpers ----------------------------------------------------------------
@@ -751,6 +787,8 @@ extern "C" int bt_adain_snake(const bt_adain_args* p) {
     return set_error(BT_EINVAL, "bt_adain_snake: gain/shift batch strides (%lld, %lld) below C = %lld",
                      (long long)p->gain_stride, (long long)p->shift_stride, (long long)p->channels);
   if (p->rows == 0) return BT_OK;
+  const int rc3 = adain_v3(p);
+  if (rc3 != BT_EUNSUPPORTED) return rc3;
   if (p->cols > kMaxRow) return set_error(BT_ETOOBIG, "bt_adain_snake: rows of %lld values exceed %d", (long long)p->cols, kMaxRow);
   size_t smem;
   int depth, rc;
@@ -777,7 +815,7 @@ extern "C" int bt_resblock_mean_leaky(const float* const* a, const float* const*
   if (n < 0) return set_error(BT_EINVAL, "bt_resblock_mean_leaky: negative size");
   if (n == 0) return BT_OK;
   m.n = n;
-  m.divisor = divisor;
+  m.rdiv = 1.0 / (double)divisor;
   m.slope = slope;
   m.out = out;
   DevInfo di;

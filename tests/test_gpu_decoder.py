@@ -57,10 +57,17 @@ def oracle_adain_snake(srcs, fc, alpha, inv, eps, snake=True):
     return env[h], env["z" if snake else "a"]
 
 
+@pytest.mark.parametrize("path", ["cluster", "one_cta"])
 @pytest.mark.parametrize("B,Cc,T,n_src,snake", [
     (1, 8, 100, 1, True), (2, 16, 4000, 2, True), (1, 4, 24001, 3, True), (3, 5, 1023, 2, False),
-    (1, 2, 7, 1, True), (2, 3, 129, 3, True), (1, 2, 2048, 1, False), (1, 3, 49152, 2, True)])
-def test_adain_snake_rows(gpu_runtime, B, Cc, T, n_src, snake):
+    (1, 2, 7, 1, True), (2, 3, 129, 3, True), (1, 2, 2048, 1, False), (1, 3, 49152, 2, True),
+    (2, 4, 24001, 1, True), (2, 4, 24001, 2, True), (1, 4, 7681, 3, False)])
+def test_adain_snake_rows(gpu_runtime, monkeypatch, path, B, Cc, T, n_src, snake):
+    """Both bt_adain_snake kernels: the cluster-split rows (default) and the
+    one-CTA-per-row kernel (BT_ADAIN_ONE_CTA=1, the fallback for requests the
+    cluster kernel does not cover)."""
+    if path == "one_cta":
+        monkeypatch.setenv("BT_ADAIN_ONE_CTA", "1")
     rt = gpu_runtime
     rng = np.random.default_rng(T + n_src)
     srcs = [(rng.standard_normal((B, Cc, T)) * 2).astype(np.float32) for _ in range(n_src)]
