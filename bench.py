@@ -455,26 +455,44 @@ def run_b200(args):
     return 0
 
 
+PROFILE_KINDS = {
+    # name: (sources, residual written, outputs)
+    "2src": (2, True, 1),      # pairs 1-2 first AdaIN: conv output + residual
+    "1src": (1, False, 1),     # second AdaIN of every pair
+    "shared3": (2, True, 3),   # the shared instance norm of the three resblocks
+}
+
+
 def run_profile_adain(args):
-    """One kind of stage-2 bt_adain_snake launch (two sources + residual +
-    snake output, the most common launch of the stream) on its own, for ncu:
-    batch x 128 rows of 24001 values, every array larger than L2."""
+    """One kind of stage-2 bt_adain_snake launch on its own, for ncu:
+    batch x 128 rows of 24001 values (every array larger than L2 from batch
+    16 up).  --profile-kind picks the launch: '2src' (two sources + residual
+    + snake output, the most common launch of the stream), '1src' (one
+    source, one snake output) or 'shared3' (two sources + residual, three
+    snake outputs)."""
     import torch
     from bt_b200.runtime import BtRuntime
     torch.cuda.set_device(0)
     rt = BtRuntime(0)
+    n_src, with_res, n_out = PROFILE_KINDS[args.profile_kind]
     B, C, T = args.batch, 128, args.t0 * 60 + 1
     g = torch.Generator(device="cuda").manual_seed(5)
-    srcs = [torch.randn((B, C, T), device="cuda", generator=g) for _ in range(2)]
-    res = torch.empty((B, C, T), device="cuda")
-    out = [torch.empty((B, C, T), device="cuda")]
-    fc = torch.randn((B, 2 * C), device="cuda", generator=g)
-    alpha = (torch.rand(C, device="cuda", generator=g) + 0.5).half()
-    inv = (1.0 / alpha.float()).half()
+    srcs = [torch.randn((B, C, T), device="cuda", generator=g) for _ in range(n_src)]
+    res = torch.empty((B, C, T), device="cuda") if with_res else None
+    out = [torch.empty((B, C, T), device="cuda") for _ in range(n_out)]
+    fc = [torch.randn((B, 2 * C), device="cuda", generator=g) for _ in range(n_out)]
+    alpha = [(torch.rand(C, device="cuda", generator=g) + 0.5).half() for _ in range(n_out)]
+    inv = [(1.0 / a.float()).half() for a in alpha]
+    gains = [f[:, :C] for f in fc]
+    shifts = [f[:, C:] for f in fc]
     for _ in range(args.warmup + args.steps):
-        rt.adain_snake(srcs, fc[:, :C], fc[:, C:], 1e-5, alpha, inv, res=res, outs=out)
+        if n_out == 1:
+            rt.adain_snake(srcs, gains[0], shifts[0], 1e-5, alpha[0], inv[0], res=res, outs=out)
+        else:
+            rt.adain_snake(srcs, gains, shifts, 1e-5, alpha, inv, res=res, outs=out)
     torch.cuda.synchronize()
-    print(json.dumps({"profile": "adain_snake stage 2, 2 sources + residual + snake", "rows": B * C, "cols": T,
+    print(json.dumps({"profile": f"adain_snake stage 2, kind {args.profile_kind}", "rows": B * C, "cols": T,
+                      "sources": n_src, "residual": with_res, "outputs": n_out,
                       "launches": args.warmup + args.steps}))
     return 0
 
@@ -492,6 +510,8 @@ def main():
     ap.add_argument("--no-per-op", action="store_true")
     ap.add_argument("--profile-adain", action="store_true",
                     help="run only stage-2 bt_adain_snake launches (for ncu)")
+    ap.add_argument("--profile-kind", default="2src", choices=sorted(PROFILE_KINDS),
+                    help="which bt_adain_snake launch --profile-adain runs")
     args = ap.parse_args()
     if args.profile_adain:
         return run_profile_adain(args)

@@ -20,12 +20,15 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <algorithm>
+#include <type_traits>
 #include <map>
 #include <mutex>
 #include <vector>
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
+#include "bt_pk.h"
 
 namespace bt {
 namespace cg = cooperative_groups;
@@ -33,25 +36,34 @@ namespace cg = cooperative_groups;
 namespace {
 
 constexpr int kMaxLeaves = 512;
+constexpr int kMaxSlots = 384;
 constexpr int kMaxIds = 1024;     // heap ids < 2^(D+1), D <= 9
 constexpr int kMaxCluster = 8;
 constexpr int kThreads = 256;
 constexpr int kMaxT = 49152;
 
-struct PlanParams {
-  int32_t T, D, n_leaf, cs;
-  int32_t rank_leaf[kMaxCluster + 1];   // first leaf of each CTA rank
+// The pairwise plan of one row length T for a cluster of cs CTAs.  Rank r
+// owns the elements [rank_e[r], rank_e[r+1]) -- whole leaves -- and the
+// slots [rank_slot[r], rank_slot[r+1]).  A slot is the work of one group of
+// eight lanes in a leaf pass: one leaf, or two leaves with the same number of
+// 8-element steps, summed side by side in the two halves of a float2.
+//   w0: offset of leaf A / 8 (bits 0-12) | offset of leaf B / 8 (13-25),
+//       both relative to rank_e[r] (B = A when the slot has one leaf)
+//   w1: heap id of A (0-9) | heap id of B (10-19, 0 = none) | steps (20-24)
+//       | A's remainder len % 8 (25-27) | B's remainder (28-30)
+struct SlotPlan {
+  int32_t T, D, cs;
+  int32_t rank_e[kMaxCluster + 1];
+  int32_t rank_slot[kMaxCluster + 1];
   uint32_t inner[kMaxIds / 32];        // bit h: heap node h is an inner node
-  uint16_t off8[kMaxLeaves];           // leaf offset / 8, leaves sorted by offset
-  uint16_t id[kMaxLeaves];             // heap id of the leaf
-  uint8_t len[kMaxLeaves];             // leaf length (<= 128)
+  uint32_t w0[kMaxSlots];
+  uint32_t w1[kMaxSlots];
 };
 
-struct AdainV3Args {
-  PlanParams P;
-  int64_t rows, channels;
+struct AdainArgs {
+  SlotPlan P;
   int64_t gain_stride, shift_stride;
-  int32_t n_src, n_out, alpha_dtype, seg_cap;
+  int32_t n_out, alpha_dtype, seg_cap;
   int32_t log2_cs, log2_c, channels32;   // log2_c < 0: channels not a power of two
   float eps;
   const float* src0;
@@ -86,134 +98,153 @@ __device__ __forceinline__ void stage_async(float* b, const float* g, int n) {
   int head = (4 - phase4(g)) & 3;
   if (head > n) head = n;
   const int nvec = (n - head) >> 2;
-  for (int q = threadIdx.x; q < nvec; q += blockDim.x) cp_async16(b + head + 4 * q, g + head + 4 * q);
-  for (int i = threadIdx.x; i < head; i += blockDim.x) b[i] = g[i];
-  for (int i = head + 4 * nvec + threadIdx.x; i < n; i += blockDim.x) b[i] = g[i];
+  for (int q = threadIdx.x; q < nvec; q += kThreads) cp_async16(b + head + 4 * q, g + head + 4 * q);
+  for (int i = threadIdx.x; i < head; i += kThreads) b[i] = g[i];
+  for (int i = head + 4 * nvec + threadIdx.x; i < n; i += kThreads) b[i] = g[i];
 }
-
-// This CTA's slice of the pairwise plan, copied from the parameter block
-// into shared memory (leaf reads are lane-divergent; shared memory serves
-// them in parallel, the constant bank would serialise them).
-struct SPlan {
-  int* off;        // local leaf offsets (relative to the segment start)
-  int* len;
-  int* id;
-  uint32_t* inner;
-  int nl;          // leaves of this CTA
-  int D;
-};
 
 // Combines the inner nodes of the tree in hs (warp 0, level by level); the
 // root hs[1] is the sum.  Only warp 0 returns with a complete tree: callers
 // read hs[1] from warp 0 (or after a barrier).
-__device__ __forceinline__ void tree_combine(float* hs, const SPlan& S) {
+__device__ __forceinline__ void tree_combine(float* hs, const uint32_t* inner, int D) {
   if (threadIdx.x < 32) {
-    for (int k = S.D - 1; k >= 0; --k) {
+    for (int k = D - 1; k >= 0; --k) {
       for (int j = threadIdx.x; j < (1 << k); j += 32) {
         const int h = (1 << k) + j;
-        if ((S.inner[h >> 5] >> (h & 31)) & 1u) hs[h] = BT_ADD(hs[2 * h], hs[2 * h + 1]);
+        if ((inner[h >> 5] >> (h & 31)) & 1u) hs[h] = BT_ADD(hs[2 * h], hs[2 * h + 1]);
       }
       __syncwarp();
     }
   }
 }
 
+__device__ __forceinline__ float2 shfl_xor2(unsigned mask, float2 v, int m) {
+  return make_float2(__shfl_xor_sync(mask, v.x, m), __shfl_xor_sync(mask, v.y, m));
+}
+
+// One leaf-sum pass over this CTA's slots.  Lane j of a slot's group owns
+// numpy's accumulator j of both leaves (elements 8m + j), so at every step
+// the group reads eight consecutive floats per leaf: the host orders slots so
+// that the four groups of a warp start in different 8-bank octets, which
+// keeps the reads free of bank conflicts.  The accumulators start at -0.0
+// (-0.0 + x == x for every x, so the first add reproduces numpy's r[j] =
+// a[j]); lanes then combine them with xor shuffles over lane bits 0, 1, 2 --
+// numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), float addition being
+// commutative -- and add the len % 8 remainder left to right (a leaf shorter
+// than 8 is the remainder alone, summed from +0.0).  Lanes j < cs write the
+// leaf sums into hs[id] of cluster rank j.
+//   pass 1 (SQ false): leaf value h = src0 (+ src1 (+ src2)); with NSRC > 1 h
+//     is also stored back into b0 for the later passes;
+//   pass 2 (SQ true, NSRC 1): (h - mu)^2.
 template <int NSRC, bool SQ>
-__device__ __forceinline__ float leaf_value(float* b0, const float* b1, const float* b2, int i, float mu,
-                                            bool store) {
-  float v = b0[i];
-  if (NSRC > 1) v = BT_ADD(v, b1[i]);
-  if (NSRC > 2) v = BT_ADD(v, b2[i]);
-  if (NSRC > 1 && store) b0[i] = v;
-  if (SQ) {
-    const float d = BT_SUB(v, mu);
-    return BT_MUL(d, d);
-  }
-  return v;
-}
-
-// Sums this CTA's leaves and writes each leaf sum into hs[id] of every CTA of
-// the cluster.  LPL lanes per leaf (2, 4 or 8) each own 8 / LPL of numpy's
-// eight accumulators (lane j owns r[j*A .. j*A + A - 1], A = 8 / LPL); the
-// accumulators are combined in numpy's bracket order
-// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) -- inside the lane first, then across
-// lanes with xor shuffles (float addition commutes).  NSRC > 1 in the first
-// pass also stores h = src0 + src1 (+ src2) back into b0.
-template <int NSRC, bool SQ, int LPL>
-__device__ __forceinline__ void leaf_pass(const SPlan& S, float* b0, const float* b1, const float* b2, float mu,
-                                          float* hs, cg::cluster_group& cluster, int cs) {
-  constexpr int APL = 8 / LPL;
-  const int j = threadIdx.x & (LPL - 1);
-  const unsigned gmask = ((1u << LPL) - 1u) << (threadIdx.x & 31 & ~(LPL - 1));
-  const bool store = (NSRC > 1) && !SQ;
-  auto lv = [&](int i) -> float { return leaf_value<NSRC, SQ>(b0, b1, b2, i, mu, store); };
-  for (int L = threadIdx.x / LPL; L < S.nl; L += blockDim.x / LPL) {
-    const int off = S.off[L];
-    const int len = S.len[L];
-    float res = 0.0f;
-    if (len < 8) {
-      if (j == 0)
-        for (int i = 0; i < len; ++i) res = BT_ADD(res, lv(off + i));
-    } else {
-      const int o = off + j * APL;
-      float r[APL];
-#pragma unroll
-      for (int a = 0; a < APL; ++a) r[a] = lv(o + a);
-      const int full = len & ~7;
-      for (int i = 8; i < full; i += 8) {
-#pragma unroll
-        for (int a = 0; a < APL; ++a) r[a] = BT_ADD(r[a], lv(o + i + a));
+__device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0, const float* b1, const float* b2,
+                                          float mu, float* hs, cg::cluster_group& cluster, int cs) {
+  const int j = threadIdx.x & 7;
+  const unsigned gmask = 0xffu << (threadIdx.x & 24);
+  const float2 nmu = pk(-mu);
+  auto lv = [&](int i) -> float {   // one leaf value, scalar (remainders)
+    float v = b0[i];
+    if (NSRC > 1) v = BT_ADD(v, b1[i]);
+    if (NSRC > 2) v = BT_ADD(v, b2[i]);
+    if (NSRC > 1 && !SQ) b0[i] = v;
+    if (SQ) {
+      const float d = BT_SUB(v, mu);
+      return BT_MUL(d, d);
+    }
+    return v;
+  };
+  for (int s = threadIdx.x >> 3; s < ns; s += kThreads >> 3) {
+    const uint32_t w0 = sw[2 * s], w1 = sw[2 * s + 1];
+    const int oa = (int)(w0 & 0x1fffu) << 3;
+    const int ob = (int)((w0 >> 13) & 0x1fffu) << 3;
+    const int steps = (int)((w1 >> 20) & 31u);
+    const int end = steps << 3;
+    float2 acc = pk(-0.0f);
+    for (int i = j; i < end; i += 8) {
+      float2 x = pk(b0[oa + i], b0[ob + i]);
+      if (NSRC > 1) {
+        x = pk_add(x, pk(b1[oa + i], b1[ob + i]));
+        if (NSRC > 2) x = pk_add(x, pk(b2[oa + i], b2[ob + i]));
+        if (!SQ) {
+          b0[oa + i] = x.x;
+          b0[ob + i] = x.y;
+        }
       }
-      float t;
-      if (APL == 4) t = BT_ADD(BT_ADD(r[0], r[1]), BT_ADD(r[2 % APL], r[3 % APL]));
-      else if (APL == 2) t = BT_ADD(r[0], r[1 % APL]);
-      else t = r[0];
-#pragma unroll
-      for (int m = 1; m < LPL; m <<= 1) t = BT_ADD(t, __shfl_xor_sync(gmask, t, m));
-      res = t;
-      if (j == 0)
-        for (int i = full; i < len; ++i) res = BT_ADD(res, lv(off + i));
+      if (SQ) {
+        const float2 d = pk_add(x, nmu);
+        acc = pk_add_lanes(acc, pk_mul(d, d));
+      } else {
+        acc = pk_add(acc, x);
+      }
     }
-    if (j == 0) {
-      const int id = S.id[L];
-      for (int rr = 0; rr < cs; ++rr) cluster.map_shared_rank(hs, rr)[id] = res;
+    acc = pk_add(acc, shfl_xor2(gmask, acc, 1));
+    acc = pk_add(acc, shfl_xor2(gmask, acc, 2));
+    acc = pk_add(acc, shfl_xor2(gmask, acc, 4));
+    if (steps == 0) acc = pk(0.0f);
+    const int ta = (int)((w1 >> 25) & 7u), tb = (int)((w1 >> 28) & 7u);
+    if (ta | tb) {
+      // one lane walks the remainders (pass 1 may store h back), then shares
+      if (j == 0) {
+        for (int t = 0; t < ta; ++t) acc.x = BT_ADD(acc.x, lv(oa + end + t));
+        for (int t = 0; t < tb; ++t) acc.y = BT_ADD(acc.y, lv(ob + end + t));
+      }
+      acc.x = __shfl_sync(gmask, acc.x, 0, 8);
+      acc.y = __shfl_sync(gmask, acc.y, 0, 8);
+    }
+    if (j < cs) {
+      float* dst = cluster.map_shared_rank(hs, j);
+      dst[w1 & 1023u] = acc.x;
+      const unsigned idb = (w1 >> 10) & 1023u;
+      if (idb) dst[idb] = acc.y;
     }
   }
 }
 
-template <int NSRC, bool SNAKE, int LPL>
-__global__ void __launch_bounds__(kThreads, 4) adain_v3_kernel(AdainV3Args A) {
+template <int NSRC, bool SNAKE>
+__global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A) {
   extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ float prm[BT_ADAIN_MAX_OUT][4];   // gain, shift, alpha, 1/alpha of this row
+  __shared__ double scal[2];                   // mean, 1/sd (double) of this row
+  __shared__ int in_range[BT_ADAIN_MAX_OUT];   // output k's sin arguments provably in range
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = A.P.cs;                 // 1, 2, 4 or 8
   const int rank = (int)cluster.block_rank();
   const int row32 = (int)(blockIdx.x >> A.log2_cs);
   const int64_t row = row32;
   const int T = A.P.T;
-  const int lb = A.P.rank_leaf[rank], le = A.P.rank_leaf[rank + 1];
-  const int e0 = 8 * (int)A.P.off8[lb];
-  const int e1 = 8 * (int)A.P.off8[le - 1] + (int)A.P.len[le - 1];
-  const int seg = e1 - e0;
+  const int e0 = A.P.rank_e[rank];
+  const int seg = A.P.rank_e[rank + 1] - e0;
+  const int sl0 = A.P.rank_slot[rank];
+  const int ns = A.P.rank_slot[rank + 1] - sl0;
   const int ids = 2 << A.P.D;
-  const int nl = le - lb;
 
-  // shared layout: hs1[ids] hs2[ids] | off[nl] len[nl] id[nl] inner[32] | sources
+  // shared layout: hs1[ids] hs2[ids] | slot words[2 ns] inner[32] | sources
   float* hs1 = (float*)smem;
   float* hs2 = hs1 + ids;
-  SPlan S;
-  S.off = (int*)(hs2 + ids);
-  S.len = S.off + nl;
-  S.id = S.len + nl;
-  S.inner = (uint32_t*)(S.id + nl);
-  S.nl = nl;
-  S.D = A.P.D;
-  for (int L = threadIdx.x; L < nl; L += blockDim.x) {
-    S.off[L] = 8 * (int)A.P.off8[lb + L] - e0;
-    S.len[L] = (int)A.P.len[lb + L];
-    S.id[L] = (int)A.P.id[lb + L];
+  uint32_t* sw = (uint32_t*)(hs2 + ids);
+  uint32_t* inner = sw + 2 * ns;
+  for (int i = threadIdx.x; i < ns; i += kThreads) {
+    sw[2 * i] = A.P.w0[sl0 + i];
+    sw[2 * i + 1] = A.P.w1[sl0 + i];
   }
-  for (int j = threadIdx.x; j < kMaxIds / 32; j += blockDim.x) S.inner[j] = A.P.inner[j];
-  float* sb = (float*)(((uintptr_t)(S.inner + kMaxIds / 32) + 15) & ~(uintptr_t)15);
+  for (int i = threadIdx.x; i < kMaxIds / 32; i += kThreads) inner[i] = A.P.inner[i];
+  const int bt = A.log2_c >= 0 ? (row32 >> A.log2_c) : row32 / A.channels32;
+  const int c = row32 - bt * A.channels32;
+#pragma unroll
+  for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
+    if (threadIdx.x == 32 * k && k < A.n_out) {
+      prm[k][0] = A.gain[k][bt * A.gain_stride + c];
+      prm[k][1] = A.shift[k][bt * A.shift_stride + c];
+      if (SNAKE) {
+        prm[k][2] = ldf(A.alpha[k], A.alpha_dtype, c);
+        prm[k][3] = ldf(A.inv_alpha[k], A.alpha_dtype, c);
+      }
+    }
+  }
+  // sources from the next 16-byte boundary; indexing smem directly (no
+  // integer round trip) keeps the pointers in the shared address space
+  const int sb_words = (2 * ids + 2 * ns + kMaxIds / 32 + 3) & ~3;
+  float* sb = reinterpret_cast<float*>(smem) + sb_words;
   const int64_t gofs = row * (int64_t)T + e0;
   const float* g0 = A.src0 + gofs;
   float* b0 = sb + phase4(g0);
@@ -226,28 +257,53 @@ __global__ void __launch_bounds__(kThreads, 4) adain_v3_kernel(AdainV3Args A) {
   if (NSRC > 1) stage_async(b1, g1, seg);
   if (NSRC > 2) stage_async(b2, g2, seg);
   cp_async_wait_all();
-  // Also guarantees every CTA of the cluster runs before any distributed
-  // shared-memory write below.
-  cluster.sync();
+  // A CTA barrier for the staged rows, the plan and the row constants; with
+  // cs > 1 also the guarantee that every CTA of the cluster runs before any
+  // distributed shared-memory write below (an arrival without release
+  // semantics suffices for that).
+  __syncthreads();
+  if (cs > 1) {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+  }
+  // Leaf sums written into other CTAs' shared memory become visible to them
+  // at a full cluster barrier (release / acquire); a cluster of one needs
+  // only the CTA barrier.
+  auto sync_sums = [&]() {
+    if (cs > 1) cluster.sync();
+    else __syncthreads();
+  };
 
-  // Per-row scalars are derived once (thread 0) and read back by all threads:
-  // scal[0] = mu, scal[1] = 1/sd in double precision (two floats' worth).
-  __shared__ double scal[2];
   // ReduceMean(h)
-  leaf_pass<NSRC, false, LPL>(S, b0, b1, b2, 0.0f, hs1, cluster, cs);
-  cluster.sync();
-  tree_combine(hs1, S);
+  slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
+  sync_sums();
+  tree_combine(hs1, inner, A.P.D);
   if (threadIdx.x == 0) scal[0] = (double)np_mean_from_sum(BT_ADD(0.0f, hs1[1]), T);
   __syncthreads();
   const float mu = (float)scal[0];
   // Sub, Mul(d, d), ReduceMean, Add eps, Sqrt
-  leaf_pass<1, true, LPL>(S, b0, nullptr, nullptr, mu, hs2, cluster, cs);
-  cluster.sync();
-  tree_combine(hs2, S);
+  slot_pass<1, true>(sw, ns, b0, nullptr, nullptr, mu, hs2, cluster, cs);
+  sync_sums();
+  tree_combine(hs2, inner, A.P.D);
   if (threadIdx.x == 0) {
     const float var = np_mean_from_sum(BT_ADD(0.0f, hs2[1]), T);
     const float sd = BT_SQRT(BT_ADD(var, A.eps));
-    scal[1] = recip_d(sd);
+    const double rsd0 = recip_d(sd);
+    scal[1] = rsd0;
+    if (SNAKE) {
+      // Every |h_i - mu|^2 is at most S = sum_j (h_j - mu)^2, whose float32
+      // pairwise sum S' has a relative error far below 2^-10; the normalised
+      // value, the affine step and the alpha product each add one rounding
+      // (factors 1 + 2^-20 below cover them).  When the bound on |alpha * y|
+      // is under half numpy's reduction range, no argument can leave it
+      // (NaN or Inf anywhere makes the bound fail and keeps the checks).
+      const double nb = sqrt((double)hs2[1] * (1.0 + 0x1p-10)) * rsd0 * (1.0 + 0x1p-20);
+      for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
+        const double zb = fabs((double)prm[k][2]) *
+                          (fabs((double)prm[k][0]) * nb + fabs((double)prm[k][1])) * (1.0 + 0x1p-20);
+        in_range[k] = (k < A.n_out && zb <= 0.5 * 117435.992) ? 1 : 0;
+      }
+    }
   }
   __syncthreads();
   const double rsd = scal[1];
@@ -260,26 +316,20 @@ __global__ void __launch_bounds__(kThreads, 4) adain_v3_kernel(AdainV3Args A) {
   if (A.res) {
     float* r = A.res + gofs;
     if (phase4(r) == phase4(g0)) {
-      for (int q = threadIdx.x; q < nvec; q += blockDim.x)
+      for (int q = threadIdx.x; q < nvec; q += kThreads)
         __stcs((float4*)(r + head + 4 * q), *(const float4*)(b0 + head + 4 * q));
-      for (int i = threadIdx.x; i < head; i += blockDim.x) r[i] = b0[i];
-      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += blockDim.x) r[i] = b0[i];
+      for (int i = threadIdx.x; i < head; i += kThreads) r[i] = b0[i];
+      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
     } else {
-      for (int i = threadIdx.x; i < seg; i += blockDim.x) r[i] = b0[i];
+      for (int i = threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
     }
   }
-  const int bt = A.log2_c >= 0 ? (row32 >> A.log2_c) : row32 / A.channels32;
-  const int c = row32 - bt * A.channels32;
+  const float2 nmu = pk(-mu);
 #pragma unroll
   for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
     if (k >= A.n_out) break;
-    const float gain = A.gain[k][bt * A.gain_stride + c];
-    const float shift = A.shift[k][bt * A.shift_stride + c];
-    float al = 0.0f, ial = 0.0f;
-    if (SNAKE) {
-      al = ldf(A.alpha[k], A.alpha_dtype, c);
-      ial = ldf(A.inv_alpha[k], A.alpha_dtype, c);
-    }
+    const float gain = prm[k][0], shift = prm[k][1];
+    const float al = SNAKE ? prm[k][2] : 0.0f, ial = SNAKE ? prm[k][3] : 0.0f;
     // Sub -> Div -> Mul(1 + gamma) -> Add(beta) [-> Mul(alpha) -> Sin -> Pow 2 -> Mul(1/alpha) -> Add]
     auto f = [&](float v) -> float {
       float y = BT_ADD(BT_MUL(gain, div_by(BT_SUB(v, mu), rsd)), shift);
@@ -289,16 +339,31 @@ __global__ void __launch_bounds__(kThreads, 4) adain_v3_kernel(AdainV3Args A) {
       }
       return y;
     };
+    // the same steps on two elements at a time; CHECKED false when the row's
+    // bound shows every sin argument in numpy's reduction range
+    auto f2 = [&](float2 v, auto checked) -> float2 {
+      const float2 a = pk_add(v, nmu);
+      const float2 n = pk(div_by(a.x, rsd), div_by(a.y, rsd));
+      float2 y = pk_add_lanes(pk_mul(pk(gain), n), pk(shift));
+      if (SNAKE)
+        y = pk_add_lanes(y, pk_mul(pk(ial), pk_np_sin<true, decltype(checked)::value>(pk_mul(pk(al), y))));
+      return y;
+    };
+    auto vec_loop = [&](float* o, auto checked) {
+      for (int q = threadIdx.x; q < nvec; q += kThreads) {
+        const float4 v = *(const float4*)(b0 + head + 4 * q);
+        const float2 lo = f2(pk(v.x, v.y), checked), hi = f2(pk(v.z, v.w), checked);
+        __stcs((float4*)(o + head + 4 * q), make_float4(lo.x, lo.y, hi.x, hi.y));
+      }
+    };
     float* o = A.out[k] + gofs;
     if (phase4(o) == phase4(g0)) {
-      for (int q = threadIdx.x; q < nvec; q += blockDim.x) {
-        const float4 v = *(const float4*)(b0 + head + 4 * q);
-        __stcs((float4*)(o + head + 4 * q), make_float4(f(v.x), f(v.y), f(v.z), f(v.w)));
-      }
-      for (int i = threadIdx.x; i < head; i += blockDim.x) o[i] = f(b0[i]);
-      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += blockDim.x) o[i] = f(b0[i]);
+      if (SNAKE && in_range[k]) vec_loop(o, std::false_type());
+      else vec_loop(o, std::true_type());
+      for (int i = threadIdx.x; i < head; i += kThreads) o[i] = f(b0[i]);
+      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) o[i] = f(b0[i]);
     } else {
-      for (int i = threadIdx.x; i < seg; i += blockDim.x) o[i] = f(b0[i]);
+      for (int i = threadIdx.x; i < seg; i += kThreads) o[i] = f(b0[i]);
     }
   }
 }
@@ -337,42 +402,147 @@ const HostPlan& host_plan(int T) {
   return cache.emplace(T, std::move(p)).first->second;
 }
 
-template <int NSRC, bool SNAKE, int LPL>
-void* kernel_ptr() { return (void*)adain_v3_kernel<NSRC, SNAKE, LPL>; }
-
-template <int LPL>
-void* pick_kernel_lpl(int nsrc, bool snake) {
-  switch (nsrc * 2 + (snake ? 1 : 0)) {
-    case 2: return kernel_ptr<1, false, LPL>();
-    case 3: return kernel_ptr<1, true, LPL>();
-    case 4: return kernel_ptr<2, false, LPL>();
-    case 5: return kernel_ptr<2, true, LPL>();
-    case 6: return kernel_ptr<3, false, LPL>();
-    default: return kernel_ptr<3, true, LPL>();
+// Leaves [first[r], first[r+1]) go to cluster rank r: contiguous runs of
+// leaves balanced by element count.  False when cs ranks cannot all get one.
+bool rank_split(const HostPlan& hp, int cs, std::vector<int>& first) {
+  const int n_leaf = (int)hp.off.size();
+  first.assign(cs + 1, 0);
+  int r = 0;
+  int64_t acc = 0;
+  for (int L = 0; L < n_leaf; ++L) {
+    acc += hp.len[L];
+    if (L == n_leaf - 1 || (acc >= (int64_t)hp.T * (r + 1) / cs && r < cs - 1)) first[++r] = L + 1;
   }
+  return r == cs;
 }
 
-void* pick_kernel(int nsrc, bool snake, int lpl) {
-  if (lpl == 2) return pick_kernel_lpl<2>(nsrc, snake);
-  if (lpl == 4) return pick_kernel_lpl<4>(nsrc, snake);
-  return pick_kernel_lpl<8>(nsrc, snake);
+// The slot plan of one (T, cs), built once and cached.
+struct ClusterPlan {
+  bool ok = false;
+  int max_seg = 0;     // longest rank segment (elements)
+  int max_slots = 0;   // most slots of one rank
+  SlotPlan P;
+};
+
+const ClusterPlan& cluster_plan(int T, int cs) {
+  static std::mutex mu;
+  static std::map<int64_t, ClusterPlan> cache;
+  const HostPlan& hp = host_plan(T);
+  std::lock_guard<std::mutex> lk(mu);
+  const int64_t key = ((int64_t)T << 4) | cs;
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  ClusterPlan cp;
+  memset(&cp.P, 0, sizeof(cp.P));
+  cp.P.T = T;
+  cp.P.D = hp.D;
+  cp.P.cs = cs;
+  for (int i = 0; i < kMaxIds / 32; ++i) cp.P.inner[i] = hp.inner[i];
+  std::vector<int> first;
+  bool ok = rank_split(hp, cs, first) && (2 << hp.D) <= kMaxIds;
+  int n_slots = 0;
+  for (int r = 0; ok && r < cs; ++r) {
+    const int lb = first[r], le = first[r + 1];
+    const int base = hp.off[lb];
+    const int end = (le < (int)hp.off.size()) ? hp.off[le] : T;
+    cp.P.rank_e[r] = base;
+    cp.P.rank_slot[r] = n_slots;
+    if (end - base > cp.max_seg) cp.max_seg = end - base;
+    // Pair leaves with the same step count (leaves of one octet first), then
+    // arrange the slots in runs of four (one warp) so that the A leaves, and
+    // the B leaves, of a run start in different bank octets where possible.
+    std::map<int, std::vector<int>> by_steps;
+    for (int L = lb; L < le; ++L) by_steps[hp.len[L] / 8].push_back(L);
+    struct Slot { int a, b; };
+    std::vector<Slot> pool;
+    auto oct = [&](int L) { return L < 0 ? -1 : (hp.off[L] / 8) & 3; };
+    for (auto& g : by_steps) {
+      std::vector<int> v = g.second;
+      std::stable_sort(v.begin(), v.end(), [&](int x, int y) { return oct(x) < oct(y); });
+      for (size_t i = 0; i < v.size(); i += 2) pool.push_back({v[i], i + 1 < v.size() ? v[i + 1] : -1});
+    }
+    std::vector<Slot> order;
+    std::vector<bool> used(pool.size(), false);
+    for (size_t done = 0; done < pool.size();) {
+      bool ua[4] = {false, false, false, false}, ub[4] = {false, false, false, false};
+      for (int g = 0; g < 4 && done < pool.size(); ++g) {
+        int best = -1, best_cost = 1 << 30;
+        for (size_t i = 0; i < pool.size(); ++i) {
+          if (used[i]) continue;
+          const int oa = oct(pool[i].a), ob = oct(pool[i].b);
+          const int cost = (ua[oa] ? 1 : 0) + (ob >= 0 && ub[ob] ? 1 : 0);
+          if (cost < best_cost) { best_cost = cost; best = (int)i; if (cost == 0) break; }
+        }
+        used[best] = true;
+        ua[oct(pool[best].a)] = true;
+        if (pool[best].b >= 0) ub[oct(pool[best].b)] = true;
+        order.push_back(pool[best]);
+        ++done;
+      }
+    }
+    if (n_slots + (int)order.size() > kMaxSlots) { ok = false; break; }
+    for (const Slot& sl : order) {
+      const int a = sl.a, b = sl.b >= 0 ? sl.b : sl.a;
+      const uint32_t oa = (uint32_t)(hp.off[a] - base) / 8, ob = (uint32_t)(hp.off[b] - base) / 8;
+      const uint32_t steps = (uint32_t)hp.len[a] / 8;
+      const uint32_t ta = (uint32_t)hp.len[a] % 8, tb = sl.b >= 0 ? (uint32_t)hp.len[b] % 8 : 0u;
+      const uint32_t idb = sl.b >= 0 ? (uint32_t)hp.id[b] : 0u;
+      if (oa >= 8192 || ob >= 8192 || steps > 16) { ok = false; break; }
+      cp.P.w0[n_slots] = oa | (ob << 13);
+      cp.P.w1[n_slots] = (uint32_t)hp.id[a] | (idb << 10) | (steps << 20) | (ta << 25) | (tb << 28);
+      ++n_slots;
+    }
+    const int rs = n_slots - cp.P.rank_slot[r];
+    if (rs > cp.max_slots) cp.max_slots = rs;
+  }
+  cp.P.rank_e[cs] = T;
+  cp.P.rank_slot[cs] = n_slots;
+  cp.ok = ok;
+  return cache.emplace(key, cp).first->second;
+}
+
+template <int NSRC, bool SNAKE>
+void* kernel_ptr() { return (void*)adain_cluster_kernel<NSRC, SNAKE>; }
+
+void* pick_kernel(int nsrc, bool snake) {
+  switch (nsrc * 2 + (snake ? 1 : 0)) {
+    case 2: return kernel_ptr<1, false>();
+    case 3: return kernel_ptr<1, true>();
+    case 4: return kernel_ptr<2, false>();
+    case 5: return kernel_ptr<2, true>();
+    case 6: return kernel_ptr<3, false>();
+    default: return kernel_ptr<3, true>();
+  }
 }
 
 std::mutex g_attr_mu;
 bool g_attr_done[64] = {false};
+size_t g_dyn_max[64] = {0};
 
-int set_attributes(int device, int max_smem) {
+// Raises every variant's dynamic shared-memory limit to what the device
+// allows beside the kernel's static shared memory; *dyn_max = the smallest
+// such limit over the variants.
+int set_attributes(int device, int max_smem, size_t* dyn_max) {
   std::lock_guard<std::mutex> lk(g_attr_mu);
   if (device < 0 || device >= 64) return set_error(BT_EUNSUPPORTED, "device ordinal %d", device);
-  if (g_attr_done[device]) return BT_OK;
-  for (int lpl = 2; lpl <= 8; lpl *= 2)
+  if (!g_attr_done[device]) {
+    size_t lim = (size_t)max_smem;
     for (int ns = 1; ns <= 3; ++ns)
       for (int sn = 0; sn < 2; ++sn) {
-        cudaError_t e = cudaFuncSetAttribute(pick_kernel(ns, sn != 0, lpl),
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+        void* fn = pick_kernel(ns, sn != 0);
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+        if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+        if (fa.sharedSizeBytes >= (size_t)max_smem) return set_error(BT_EUNSUPPORTED, "static shared memory");
+        const size_t dyn = (size_t)max_smem - fa.sharedSizeBytes;
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
         if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        if (dyn < lim) lim = dyn;
       }
-  g_attr_done[device] = true;
+    g_dyn_max[device] = lim;
+    g_attr_done[device] = true;
+  }
+  *dyn_max = g_dyn_max[device];
   return BT_OK;
 }
 
@@ -396,73 +566,38 @@ int adain_v3(const bt_adain_args* p) {
   if (rc) return rc;
   // Smallest cluster whose per-CTA segment of all sources fits ~80 KB.
   const int ids = 2 << hp.D;
-  int cs = 1;
+  const ClusterPlan* cp = nullptr;
   size_t smem = 0;
   int seg_cap = 0;
-  for (cs = 1; cs <= kMaxCluster; cs *= 2) {
-    if (cs > n_leaf) return BT_EUNSUPPORTED;
-    // balance leaves by element count
-    int max_seg = 0, r = 0, start = 0, acc = 0;
-    for (int L = 0; L < n_leaf; ++L) {
-      acc += hp.len[L];
-      const bool last = L == n_leaf - 1;
-      if (last || (acc >= (int64_t)T * (r + 1) / cs && r < cs - 1)) {
-        const int seg = hp.off[L] + hp.len[L] - hp.off[start];
-        if (seg > max_seg) max_seg = seg;
-        start = L + 1;
-        ++r;
-      }
-    }
-    if (r != cs) continue;
-    seg_cap = ((max_seg + 4 + 3) / 4) * 4;
-    smem = (size_t)2 * ids * sizeof(float) + (size_t)3 * n_leaf * sizeof(int) + (kMaxIds / 32) * 4 + 16 +
+  for (int cs = 1; cs <= kMaxCluster; cs *= 2) {
+    if (cs > n_leaf) break;
+    const ClusterPlan& c = cluster_plan(T, cs);
+    if (!c.ok) continue;
+    cp = &c;
+    seg_cap = ((c.max_seg + 4 + 3) / 4) * 4;
+    smem = (size_t)2 * ids * sizeof(float) + (size_t)(2 * c.max_slots + kMaxIds / 32) * sizeof(uint32_t) + 16 +
            (size_t)p->n_src * seg_cap * sizeof(float);
-    if (smem <= 80 * 1024 || cs == kMaxCluster) break;
+    if (smem <= 80 * 1024) break;
   }
-  if (cs > kMaxCluster || smem > (size_t)di.max_smem_optin) return BT_EUNSUPPORTED;
+  size_t dyn_max = 0;
+  if ((rc = set_attributes(di.device, di.max_smem_optin, &dyn_max))) return rc;
+  if (!cp || smem > dyn_max) return BT_EUNSUPPORTED;
+  const int cs = cp->P.cs;
+  if (p->rows > 0x7fffffff / cs || p->channels > 0x7fffffff) return BT_EUNSUPPORTED;
 
-  AdainV3Args A;
+  AdainArgs A;
   memset(&A, 0, sizeof(A));
-  A.P.T = T;
-  A.P.D = hp.D;
-  A.P.n_leaf = n_leaf;
-  A.P.cs = cs;
-  for (int i = 0; i < kMaxIds / 32; ++i) A.P.inner[i] = hp.inner[i];
-  for (int L = 0; L < n_leaf; ++L) {
-    A.P.off8[L] = (uint16_t)(hp.off[L] / 8);
-    A.P.id[L] = (uint16_t)hp.id[L];
-    A.P.len[L] = (uint8_t)hp.len[L];
-  }
-  {
-    int r = 0, acc = 0;
-    A.P.rank_leaf[0] = 0;
-    for (int L = 0; L < n_leaf; ++L) {
-      acc += hp.len[L];
-      if (L == n_leaf - 1 || (acc >= (int64_t)T * (r + 1) / cs && r < cs - 1)) A.P.rank_leaf[++r] = L + 1;
-    }
-    if (r != cs) return BT_EUNSUPPORTED;
-  }
-  A.rows = p->rows;
-  A.channels = p->channels;
+  A.P = cp->P;
   A.gain_stride = p->gain_stride;
   A.shift_stride = p->shift_stride;
-  A.n_src = p->n_src;
   A.n_out = p->n_out;
   A.alpha_dtype = p->alpha_dtype;
   A.seg_cap = seg_cap;
   A.log2_cs = cs == 1 ? 0 : cs == 2 ? 1 : cs == 4 ? 2 : 3;
-  if (p->rows > 0x7fffffff / cs || p->channels > 0x7fffffff) return BT_EUNSUPPORTED;
   A.channels32 = (int)p->channels;
   A.log2_c = -1;
   for (int b = 0; b < 31; ++b)
     if ((1ll << b) == p->channels) A.log2_c = b;
-  int max_nl = 0;
-  for (int r = 0; r < cs; ++r) {
-    const int nl = A.P.rank_leaf[r + 1] - A.P.rank_leaf[r];
-    if (nl > max_nl) max_nl = nl;
-  }
-  // lanes per leaf: enough leaves in flight to occupy the CTA
-  const int lpl = (max_nl * 8 <= kThreads) ? 8 : (max_nl * 4 <= kThreads) ? 4 : 2;
   A.eps = p->eps;
   A.src0 = p->src[0];
   A.src1 = p->n_src > 1 ? p->src[1] : nullptr;
@@ -475,8 +610,6 @@ int adain_v3(const bt_adain_args* p) {
     A.inv_alpha[k] = p->inv_alpha[k];
     A.out[k] = p->out[k];
   }
-  if ((rc = set_attributes(di.device, di.max_smem_optin))) return rc;
-
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)(p->rows * cs), 1, 1);
@@ -491,7 +624,7 @@ int adain_v3(const bt_adain_args* p) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {(void*)&A};
-  cudaError_t e = cudaLaunchKernelExC(&cfg, pick_kernel(p->n_src, snake, lpl), args);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, pick_kernel(p->n_src, snake), args);
   if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_adain_snake(cluster): %s", cudaGetErrorString(e));
   return check_launch("bt_adain_snake(cluster)");
 }

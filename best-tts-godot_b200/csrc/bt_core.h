@@ -289,13 +289,24 @@ BT_COLD double bt_sincos_d(double x, bool cosine) {
 // (sine) or 71476.0625 (cosine) numpy falls back to the C library; there
 // bt_sincos_d (double precision, rounded to float) stands in for it.
 // ---------------------------------------------------------------------------
-BT_HD float np_sincosf(float x, bool cosine) {
+// NaN and the arguments numpy hands to the C library, kept out of line so
+// the common path stays small.
+BT_COLD float np_sincosf_big(float x, bool cosine) {
   if (is_nan(x)) return qnan();
+  return (float)bt_sincos_d((double)x, cosine);
+}
+
+// The quadrant q = t - 1.5*2^23 of t = fma(x, 2/pi, 1.5*2^23) is an integer
+// with |q| < 2^22, so t lies in [2^23, 2^24) where its ulp is 1 and the low
+// mantissa bits of t are q modulo 2^22: the two low bits of t are q mod 4,
+// the same as (int)q & 3 -- read from the bits instead of converting.
+BT_HD float np_sincosf(float x, bool cosine) {
   const float lim = cosine ? 71476.0625f : 117435.992f;
-  if (!(fabsf(x) <= lim)) return (float)bt_sincos_d((double)x, cosine);
+  if (!(fabsf(x) <= lim)) return np_sincosf_big(x, cosine);
   const float kTwoOverPi = 0x1.45f306p-1f;
   const float kMagic = 12582912.0f;
-  float q = BT_SUB(BT_FMA(x, kTwoOverPi, kMagic), kMagic);
+  const float t = BT_FMA(x, kTwoOverPi, kMagic);
+  const float q = BT_SUB(t, kMagic);
   float r = BT_FMA(q, -0x1.921fb0p+00f, x);
   r = BT_FMA(q, -0x1.5110b4p-22f, r);
   r = BT_FMA(q, -0x1.846988p-48f, r);
@@ -309,9 +320,9 @@ BT_HD float np_sincosf(float x, bool cosine) {
   s = BT_FMA(s, r2, -0x1.555556p-03f);
   s = BT_FMA(s, r2, 0.0f);
   s = BT_FMA(s, r, r);
-  int iq = (int)q + (cosine ? 1 : 0);
-  float v = ((iq & 1) == 0) ? s : c;
-  if ((iq & 2) == 2) v = BT_SUB(0.0f, v);
+  const uint32_t iq = f_bits(t) + (cosine ? 1u : 0u);
+  float v = (iq & 1u) ? c : s;
+  if (iq & 2u) v = BT_SUB(0.0f, v);
   return v;
 }
 BT_HD float np_sinf(float x) { return np_sincosf(x, false); }

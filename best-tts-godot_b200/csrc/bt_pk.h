@@ -1,0 +1,103 @@
+// bt_pk.h -- two-lane (float2) forms of the numpy-exact float32 math, for
+// sm_100a kernels.
+//
+// sm_100 executes add / multiply / fused multiply-add on a pair of floats in
+// one instruction (PTX add / mul / fma .rn.f32x2).  Each lane is rounded
+// exactly like the scalar __fadd_rn / __fmul_rn / __fmaf_rn, so a function
+// below gives, lane by lane, the same bits as its scalar original in
+// bt_core.h while issuing half the arithmetic instructions.  Subtraction is
+// written as addition of the negated operand, which IEEE 754 defines to be
+// the same operation.
+#pragma once
+#include <cuda_runtime.h>
+#include "bt_core.h"
+
+namespace bt {
+
+__device__ __forceinline__ float2 pk(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 pk(float a, float b) { return make_float2(a, b); }
+
+// The packed operations are issued as PTX with an explicit .rn rounding
+// modifier.  Even so, the compiler (CUDA 12.9, --fmad=false) fuses a packed
+// multiply whose result feeds a packed add into one packed fused
+// multiply-add -- one rounding instead of two, which changes results in a few
+// percent of cases.  So a sum that takes a packed product as an operand goes
+// through pk_add_lanes (two scalar __fadd_rn, never contracted); pk_add is
+// only for operands that are not products.
+__device__ __forceinline__ float2 pk_add(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+// a + b lane by lane with scalar adds: for sums with a packed product as an
+// operand (see above).
+__device__ __forceinline__ float2 pk_add_lanes(float2 a, float2 b) {
+  return make_float2(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 pk_mul(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 pk_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// Both lanes through the scalar function (arguments numpy does not reduce
+// itself, and NaN); out of line, it is almost never taken.
+template <bool SQUARE>
+__device__ __noinline__ float2 pk_sin_big(float2 z) {
+  float a = np_sinf(z.x), b = np_sinf(z.y);
+  if (SQUARE) {
+    a = BT_MUL(a, a);
+    b = BT_MUL(b, b);
+  }
+  return make_float2(a, b);
+}
+
+// sin of both lanes (np_sincosf with cosine = false).  With SQUARE the result
+// is sin(z)^2 as numpy's Pow(Sin(z), 2) computes it: the quadrant's sign flip
+// cannot change a square (0 - v and v square to the same float, zeros
+// included), so it is left out.
+// CHECKED false: the caller guarantees |z| <= 117435.992 (numpy's own
+// reduction range) for both lanes, so the out-of-range test is skipped.
+template <bool SQUARE, bool CHECKED = true>
+__device__ __forceinline__ float2 pk_np_sin(float2 z) {
+  const float lim = 117435.992f;
+  if (CHECKED && (!(fabsf(z.x) <= lim) || !(fabsf(z.y) <= lim))) return pk_sin_big<SQUARE>(z);
+  const float2 t = pk_fma(z, pk(0x1.45f306p-1f), pk(12582912.0f));
+  const float2 q = pk_add(t, pk(-12582912.0f));
+  float2 r = pk_fma(q, pk(-0x1.921fb0p+00f), z);
+  r = pk_fma(q, pk(-0x1.5110b4p-22f), r);
+  r = pk_fma(q, pk(-0x1.846988p-48f), r);
+  const float2 r2 = pk_mul(r, r);
+  float2 c = pk_fma(pk(0x1.98e616p-16f), r2, pk(-0x1.6c06dcp-10f));
+  c = pk_fma(c, r2, pk(0x1.55553cp-05f));
+  c = pk_fma(c, r2, pk(-0x1.000000p-01f));
+  c = pk_fma(c, r2, pk(0x1.000000p+00f));
+  float2 s = pk_fma(pk(0x1.7d3bbcp-19f), r2, pk(-0x1.a06bbap-13f));
+  s = pk_fma(s, r2, pk(0x1.11119ap-07f));
+  s = pk_fma(s, r2, pk(-0x1.555556p-03f));
+  s = pk_fma(s, r2, pk(0.0f));
+  s = pk_fma(s, r, r);
+  // low two bits of t = quadrant mod 4 (see np_sincosf)
+  const uint32_t qx = __float_as_uint(t.x), qy = __float_as_uint(t.y);
+  float2 v = make_float2((qx & 1u) ? c.x : s.x, (qy & 1u) ? c.y : s.y);
+  if (SQUARE) return pk_mul(v, v);
+  if (qx & 2u) v.x = BT_SUB(0.0f, v.x);
+  if (qy & 2u) v.y = BT_SUB(0.0f, v.y);
+  return v;
+}
+
+}  // namespace bt

@@ -88,6 +88,39 @@ def test_adain_snake_rows(gpu_runtime, monkeypatch, path, B, Cc, T, n_src, snake
         assert_same(res, h_want, "residual")
 
 
+@pytest.mark.parametrize("path", ["cluster", "one_cta"])
+@pytest.mark.parametrize("n_src", [1, 2])
+def test_adain_snake_large_and_nonfinite_rows(gpu_runtime, monkeypatch, path, n_src):
+    """Rows whose snake arguments leave numpy's sin reduction range (gain up
+    to ~1e5, so alpha * y passes 117435.992 and takes the library fallback),
+    plus rows holding a NaN or an Inf: the kernels' per-row range bound must
+    fail for these and keep the checked sin, which still matches numpy."""
+    if path == "one_cta":
+        monkeypatch.setenv("BT_ADAIN_ONE_CTA", "1")
+    rt = gpu_runtime
+    rng = np.random.default_rng(77 + n_src)
+    B, Cc, T = 2, 6, 3001
+    srcs = [(rng.standard_normal((B, Cc, T)) * 2).astype(np.float32) for _ in range(n_src)]
+    srcs[0][0, 1, 17] = np.nan
+    srcs[0][1, 2, 2900] = np.inf
+    fc = rng.standard_normal((B, 2 * Cc, 1)).astype(np.float32)
+    fc[:, :Cc] *= np.float32(6.0e4)     # gamma, hence the gain, up to ~2e5
+    alpha = rng.uniform(0.5, 1.5, (1, Cc, 1)).astype(np.float16)
+    inv = (1.0 / alpha.astype(np.float64)).astype(np.float16)
+    eps = np.array(1e-5, np.float16)
+    h_want, z_want = oracle_adain_snake(srcs, fc, alpha, inv, eps, True)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    fcd = d(fc[:, :, 0])
+    gain = rt.elementwise("ADD", [fcd[:, :Cc], d(np.array(1.0, np.float16))], (B, Cc), np.float32, np.float32)
+    res = torch.empty((B, Cc, T), dtype=torch.float32, device="cuda") if n_src > 1 else None
+    out = rt.adain_snake([d(s) for s in srcs], gain, fcd[:, Cc:], np.float32(eps), d(alpha.reshape(-1)),
+                         d(inv.reshape(-1)), res=res)
+    torch.cuda.synchronize()
+    assert_same(out[0], z_want, "adain/snake output")
+    if res is not None:
+        assert_same(res, h_want, "residual")
+
+
 def test_adain_three_outputs_share_norm(gpu_runtime):
     rt = gpu_runtime
     rng = np.random.default_rng(5)
