@@ -66,6 +66,7 @@ struct AdainArgs {
   int32_t n_out, alpha_dtype, seg_cap;
   int32_t log2_cs, log2_c, channels32;   // log2_c < 0: channels not a power of two
   float eps;
+  double rT;                             // RN64(1 / T)
   const float* src0;
   const float* src1;
   const float* src2;
@@ -160,14 +161,22 @@ __device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0,
     const int steps = (int)((w1 >> 20) & 31u);
     const int end = steps << 3;
     float2 acc = pk(-0.0f);
-    for (int i = j; i < end; i += 8) {
-      float2 x = pk(b0[oa + i], b0[ob + i]);
+    float* pa0 = b0 + oa + j;
+    float* pb0 = b0 + ob + j;
+    const float* pa1 = NSRC > 1 ? b1 + oa + j : nullptr;
+    const float* pb1 = NSRC > 1 ? b1 + ob + j : nullptr;
+    const float* pa2 = NSRC > 2 ? b2 + oa + j : nullptr;
+    const float* pb2 = NSRC > 2 ? b2 + ob + j : nullptr;
+#pragma unroll 4
+    for (int m = 0; m < steps; ++m) {
+      const int i = 8 * m;
+      float2 x = pk(pa0[i], pb0[i]);
       if (NSRC > 1) {
-        x = pk_add(x, pk(b1[oa + i], b1[ob + i]));
-        if (NSRC > 2) x = pk_add(x, pk(b2[oa + i], b2[ob + i]));
+        x = pk_add(x, pk(pa1[i], pb1[i]));
+        if (NSRC > 2) x = pk_add(x, pk(pa2[i], pb2[i]));
         if (!SQ) {
-          b0[oa + i] = x.x;
-          b0[ob + i] = x.y;
+          pa0[i] = x.x;
+          pb0[i] = x.y;
         }
       }
       if (SQ) {
@@ -278,7 +287,9 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
   sync_sums();
   tree_combine(hs1, inner, A.P.D);
-  if (threadIdx.x == 0) scal[0] = (double)np_mean_from_sum(BT_ADD(0.0f, hs1[1]), T);
+  // np.mean: RN32(RN64(sum) / T), computed as RN32(RN64(sum * RN64(1/T)))
+  // -- the same float (division by a per-row constant, see div_by)
+  if (threadIdx.x == 0) scal[0] = (double)div_by(BT_ADD(0.0f, hs1[1]), A.rT);
   __syncthreads();
   const float mu = (float)scal[0];
   // Sub, Mul(d, d), ReduceMean, Add eps, Sqrt
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   sync_sums();
   tree_combine(hs2, inner, A.P.D);
   if (threadIdx.x == 0) {
-    const float var = np_mean_from_sum(BT_ADD(0.0f, hs2[1]), T);
+    const float var = div_by(BT_ADD(0.0f, hs2[1]), A.rT);
     const float sd = BT_SQRT(BT_ADD(var, A.eps));
     const double rsd0 = recip_d(sd);
     scal[1] = rsd0;
@@ -350,6 +361,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
       return y;
     };
     auto vec_loop = [&](float* o, auto checked) {
+#pragma unroll 2
       for (int q = threadIdx.x; q < nvec; q += kThreads) {
         const float4 v = *(const float4*)(b0 + head + 4 * q);
         const float2 lo = f2(pk(v.x, v.y), checked), hi = f2(pk(v.z, v.w), checked);
@@ -599,6 +611,7 @@ int adain_v3(const bt_adain_args* p) {
   for (int b = 0; b < 31; ++b)
     if ((1ll << b) == p->channels) A.log2_c = b;
   A.eps = p->eps;
+  A.rT = 1.0 / (double)T;
   A.src0 = p->src[0];
   A.src1 = p->n_src > 1 ? p->src[1] : nullptr;
   A.src2 = p->n_src > 2 ? p->src[2] : nullptr;
