@@ -291,9 +291,10 @@ def per_op(rt, torch, peak):
     # >= 256 MB sweep
     n = 64 * 1024 * 1024
     A = torch.randn((8192, 8192), device="cuda")
+    A2 = torch.randn((8192, 8192), device="cuda")
     Bv = torch.randn((8192, 1), device="cuda")
     sweep = {}
-    for nm, op, ins, nb in [("add_rowbcast", "ADD", [A, Bv], 2 * n * 4 + 8192 * 4), ("mul_same", "MUL", [A, A], 3 * n * 4),
+    for nm, op, ins, nb in [("add_rowbcast", "ADD", [A, Bv], 2 * n * 4 + 8192 * 4), ("mul_same_shape", "MUL", [A, A2], 3 * n * 4),
                             ("sigmoid", "SIGMOID", [A], 2 * n * 4), ("tanh", "TANH", [A], 2 * n * 4),
                             ("leakyrelu", "LEAKYRELU", [A], 2 * n * 4), ("sin", "SIN", [A], 2 * n * 4),
                             ("exp", "EXP", [A], 2 * n * 4)]:

@@ -18,6 +18,7 @@
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
+#include "bt_pk.h"
 
 namespace bt {
 namespace {
@@ -138,6 +139,10 @@ __device__ __forceinline__ float np_fast_gelu(float x) {
   return BT_MUL(a, BT_ADD(1.0f, g));
 }
 
+// TRIG false: sine and cosine never reach this call (the vector kernels run
+// them in their own specialisations), so their out-of-line fallback is not
+// linked into the runtime-op kernels.
+template <bool TRIG = true>
 __device__ __forceinline__ float apply_f32(int op, float a, float b, float c, float alpha, int n_in) {
   switch (op) {
     case BT_OP_ADD: return BT_ADD(a, b);
@@ -147,8 +152,8 @@ __device__ __forceinline__ float apply_f32(int op, float a, float b, float c, fl
     case BT_OP_POW: return np_powf(a, b);
     case BT_OP_SQRT: return BT_SQRT(a);
     case BT_OP_EXP: return np_expf(a);
-    case BT_OP_SIN: return np_sinf(a);
-    case BT_OP_COS: return np_cosf(a);
+    case BT_OP_SIN: return TRIG ? np_sinf(a) : a;
+    case BT_OP_COS: return TRIG ? np_cosf(a) : a;
     case BT_OP_ATAN: return (float)atan((double)a);
     case BT_OP_TANH: return (float)tanh((double)a);
     case BT_OP_SIGMOID: return np_sigmoidf(a);
@@ -309,6 +314,28 @@ __device__ __forceinline__ void ld_vec(const Operand& o, int64_t base, float* x)
   }
 }
 
+// OP >= 0: the op is fixed at compile time (the switch in apply_f32 folds
+// away); OP < 0: the op is read from the arguments.
+template <int OP, bool TRIG = true>
+__device__ __forceinline__ float apply_op(const EwArgs& a, float x, float y, float z) {
+  return apply_f32<TRIG>(OP >= 0 ? OP : a.op, x, y, z, a.alpha, a.n_in);
+}
+
+// Four results of one vector (operands k = 0..2, elements j = 0..3).  Sine
+// and cosine run two elements per instruction (bt_pk.h); every other op goes
+// element by element.
+template <int OP>
+__device__ __forceinline__ float4 apply_vec4(const EwArgs& a, float4 x, float4 y, float4 z) {
+  if (OP == BT_OP_SIN || OP == BT_OP_COS) {
+    const float2 lo = pk_np_sincos<OP == BT_OP_COS>(make_float2(x.x, x.y));
+    const float2 hi = pk_np_sincos<OP == BT_OP_COS>(make_float2(x.z, x.w));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  return make_float4(apply_op<OP>(a, x.x, y.x, z.x), apply_op<OP>(a, x.y, y.y, z.y), apply_op<OP>(a, x.z, y.z, z.z),
+                     apply_op<OP>(a, x.w, y.w, z.w));
+}
+__device__ __forceinline__ float4 f4(const float (&v)[4]) { return make_float4(v[0], v[1], v[2], v[3]); }
+
 template <int VEC>
 __global__ void __launch_bounds__(256) ew_flat_kernel(EwArgs a) {
   const int64_t nv = a.n / VEC;
@@ -354,6 +381,63 @@ __global__ void __launch_bounds__(256) ew_flat_kernel(EwArgs a) {
     float x1 = a.n_in > 1 ? ld1<float>(a.in[1].p, a.in[1].dt, off[1]) : 0.f;
     float x2 = a.n_in > 2 ? ld1<float>(a.in[2].p, a.in[2].dt, off[2]) : 0.f;
     st1<float>(a.out, a.odt, i, apply_f32(a.op, x0, x1, x2, a.alpha, a.n_in));
+  }
+}
+
+// The same with the op fixed at compile time (OP >= 0, VEC = 4).
+template <int VEC, int OP>
+__global__ void __launch_bounds__(256) ew_flat_op_kernel(EwArgs a) {
+  constexpr bool kTrig = !(VEC == 4 && OP < 0);   // see apply_f32
+  const int64_t nv = a.n / VEC;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // U vectors per thread per iteration, all loads issued before the math.
+  // (one vector at a time where a call to an out-of-line path would
+  // otherwise need a stack frame)
+  constexpr int U = (OP == BT_OP_DIV || OP == BT_OP_SIGMOID) ? 1 : 2;
+  for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
+    float x[U][3][VEC];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v < nv) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          if (k < a.n_in) ld_vec<VEC>(a.in[k], v * VEC, x[u][k]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v >= nv) break;
+      const int64_t base = v * VEC;
+      float r[VEC];
+      if constexpr (VEC == 4 && OP >= 0) {
+        const float4 v4 = apply_vec4<OP>(a, f4(x[u][0]), a.n_in > 1 ? f4(x[u][1]) : make_float4(0.f, 0.f, 0.f, 0.f),
+                                         a.n_in > 2 ? f4(x[u][2]) : make_float4(0.f, 0.f, 0.f, 0.f));
+        r[0] = v4.x; r[1] = v4.y; r[2] = v4.z; r[3] = v4.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          r[j] = apply_op<OP, kTrig>(a, x[u][0][j], a.n_in > 1 ? x[u][1][j] : 0.f, a.n_in > 2 ? x[u][2][j] : 0.f);
+      }
+      if (VEC == 4 && a.odt == BT_F32) {
+        __stcs((float4*)((float*)a.out + base), make_float4(r[0], r[1], r[2], r[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, base + j, r[j]);
+      }
+    }
+  }
+  // tail
+  const int64_t t0 = nv * VEC;
+  const int64_t i = t0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < a.n) {
+    int64_t off[3];
+    for (int k = 0; k < 3; ++k) off[k] = i * a.in[k].st[0];
+    float x0 = ld1<float>(a.in[0].p, a.in[0].dt, off[0]);
+    float x1 = a.n_in > 1 ? ld1<float>(a.in[1].p, a.in[1].dt, off[1]) : 0.f;
+    float x2 = a.n_in > 2 ? ld1<float>(a.in[2].p, a.in[2].dt, off[2]) : 0.f;
+    st1<float>(a.out, a.odt, i, apply_op<OP, kTrig>(a, x0, x1, x2));
   }
 }
 
@@ -409,6 +493,64 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(EwArgs a) {
   }
 }
 
+// The same with the op fixed at compile time (OP >= 0, VEC = 4).
+template <int VEC, int OP>
+__global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
+  constexpr bool kTrig = !(VEC == 4 && OP < 0);   // see apply_f32
+  const int64_t R = a.shape[0], T = a.shape[1];
+  const int64_t nv = T / VEC;
+  for (int64_t r = blockIdx.y; r < R; r += gridDim.y) {
+    float rowv[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      if (k < a.n_in && a.in[k].st[1] == 0) rowv[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0]);
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = v * VEC;
+      float x[3][VEC];
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        if (k >= a.n_in) break;
+        const Operand& o = a.in[k];
+        if (o.st[1] == 0) {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) x[k][j] = rowv[k];
+        } else if (VEC == 4 && o.dt == BT_F32) {
+          float4 f = (o.st[0] == 0) ? __ldg((const float4*)((const float*)o.p + t))
+                                    : __ldcs((const float4*)((const float*)o.p + r * o.st[0] + t));
+          x[k][0] = f.x; x[k][1] = f.y; x[k][2] = f.z; x[k][3] = f.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) x[k][j] = ld1<float>(o.p, o.dt, r * o.st[0] + t + j);
+        }
+      }
+      float res[VEC];
+      if constexpr (VEC == 4 && OP >= 0) {
+        const float4 v4 = apply_vec4<OP>(a, f4(x[0]), a.n_in > 1 ? f4(x[1]) : make_float4(0.f, 0.f, 0.f, 0.f),
+                                         a.n_in > 2 ? f4(x[2]) : make_float4(0.f, 0.f, 0.f, 0.f));
+        res[0] = v4.x; res[1] = v4.y; res[2] = v4.z; res[3] = v4.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          res[j] = apply_op<OP, kTrig>(a, x[0][j], a.n_in > 1 ? x[1][j] : 0.f, a.n_in > 2 ? x[2][j] : 0.f);
+      }
+      const int64_t ob = r * a.ost[0] + t;
+      if (VEC == 4 && a.odt == BT_F32) {
+        __stcs((float4*)((float*)a.out + ob), make_float4(res[0], res[1], res[2], res[3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, ob + j, res[j]);
+      }
+    }
+    // tail of the row
+    for (int64_t t = nv * VEC + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < T;
+         t += (int64_t)gridDim.x * blockDim.x) {
+      float x[3] = {0.f, 0.f, 0.f};
+      for (int k = 0; k < a.n_in; ++k) x[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0] + t * a.in[k].st[1]);
+      st1<float>(a.out, a.odt, r * a.ost[0] + t, apply_op<OP, kTrig>(a, x[0], x[1], x[2]));
+    }
+  }
+}
+
 // ---- launch helpers ---------------------------------------------------------------
 int grid_for(int64_t work, int threads) {
   DevInfo di;
@@ -419,6 +561,32 @@ int grid_for(int64_t work, int threads) {
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   return (int)blocks;
+}
+
+// The fp32 ops with their own compiled vector kernels (the decoder stream's
+// and the per-op configurations' ops); the rest share the runtime-op kernel.
+#define BT_EW_FIXED_OPS(X) \
+  X(BT_OP_ADD) X(BT_OP_SUB) X(BT_OP_MUL) X(BT_OP_DIV) X(BT_OP_POW) X(BT_OP_SQRT) X(BT_OP_EXP) X(BT_OP_SIN) \
+  X(BT_OP_COS) X(BT_OP_TANH) X(BT_OP_SIGMOID) X(BT_OP_LEAKYRELU) X(BT_OP_GELU) X(BT_OP_IDENTITY)
+
+void launch_flat4(int op, int grid, int threads, cudaStream_t s, const EwArgs& a) {
+  switch (op) {
+#define BT_CASE(OPC) \
+  case OPC: ew_flat_op_kernel<4, OPC><<<grid, threads, 0, s>>>(a); return;
+    BT_EW_FIXED_OPS(BT_CASE)
+#undef BT_CASE
+    default: ew_flat_kernel<4><<<grid, threads, 0, s>>>(a); return;
+  }
+}
+
+void launch_rows4(int op, dim3 grid, int threads, cudaStream_t s, const EwArgs& a) {
+  switch (op) {
+#define BT_CASE(OPC) \
+  case OPC: ew_rows_op_kernel<4, OPC><<<grid, threads, 0, s>>>(a); return;
+    BT_EW_FIXED_OPS(BT_CASE)
+#undef BT_CASE
+    default: ew_rows_kernel<4><<<grid, threads, 0, s>>>(a); return;
+  }
 }
 
 bool aligned_run(const void* p, int dt, int vec) {
@@ -486,7 +654,7 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
       if (a.in[k].st[0] == 1 && !aligned_run(a.in[k].p, a.in[k].dt, 4)) vec_ok = false;
     }
     if (unit) {
-      if (vec_ok) ew_flat_kernel<4><<<grid_for((a.n + 3) / 4, threads), threads, 0, s>>>(a);
+      if (vec_ok) launch_flat4(op, grid_for((a.n + 3) / 4, threads), threads, s, a);
       else ew_flat_kernel<1><<<grid_for(a.n, threads), threads, 0, s>>>(a);
       return check_launch("bt_elementwise(flat)");
     }
@@ -504,7 +672,7 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
       int gy = (int)(p.shape[0] < 65535 ? p.shape[0] : 65535);
       int gx = (int)(per_row > 64 ? 64 : per_row);
       dim3 grid(gx, gy);
-      if (vec_ok) ew_rows_kernel<4><<<grid, threads, 0, s>>>(a);
+      if (vec_ok) launch_rows4(op, grid, threads, s, a);
       else ew_rows_kernel<1><<<grid, threads, 0, s>>>(a);
       return check_launch("bt_elementwise(rows)");
     }

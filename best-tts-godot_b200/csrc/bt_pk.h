@@ -56,9 +56,9 @@ __device__ __forceinline__ float2 pk_fma(float2 a, float2 b, float2 c) {
 
 // Both lanes through the scalar function (arguments numpy does not reduce
 // itself, and NaN); out of line, it is almost never taken.
-template <bool SQUARE>
-__device__ __noinline__ float2 pk_sin_big(float2 z) {
-  float a = np_sinf(z.x), b = np_sinf(z.y);
+template <bool COS, bool SQUARE>
+__device__ __noinline__ float2 pk_sincos_big(float2 z) {
+  float a = np_sincosf(z.x, COS), b = np_sincosf(z.y, COS);
   if (SQUARE) {
     a = BT_MUL(a, a);
     b = BT_MUL(b, b);
@@ -66,16 +66,16 @@ __device__ __noinline__ float2 pk_sin_big(float2 z) {
   return make_float2(a, b);
 }
 
-// sin of both lanes (np_sincosf with cosine = false).  With SQUARE the result
-// is sin(z)^2 as numpy's Pow(Sin(z), 2) computes it: the quadrant's sign flip
-// cannot change a square (0 - v and v square to the same float, zeros
-// included), so it is left out.
-// CHECKED false: the caller guarantees |z| <= 117435.992 (numpy's own
-// reduction range) for both lanes, so the out-of-range test is skipped.
-template <bool SQUARE, bool CHECKED = true>
-__device__ __forceinline__ float2 pk_np_sin(float2 z) {
-  const float lim = 117435.992f;
-  if (CHECKED && (!(fabsf(z.x) <= lim) || !(fabsf(z.y) <= lim))) return pk_sin_big<SQUARE>(z);
+// sin (COS false) or cos (COS true) of both lanes, np_sincosf step for step.
+// With SQUARE the result is the square as numpy's Pow(., 2) computes it: the
+// quadrant's sign flip cannot change a square (0 - v and v square to the
+// same float, zeros included), so it is left out.  CHECKED false: the caller
+// guarantees |z| <= 117435.992 (sine) or 71476.0625 (cosine) -- numpy's own
+// reduction range -- for both lanes, so the out-of-range test is skipped.
+template <bool COS, bool SQUARE = false, bool CHECKED = true>
+__device__ __forceinline__ float2 pk_np_sincos(float2 z) {
+  const float lim = COS ? 71476.0625f : 117435.992f;
+  if (CHECKED && (!(fabsf(z.x) <= lim) || !(fabsf(z.y) <= lim))) return pk_sincos_big<COS, SQUARE>(z);
   const float2 t = pk_fma(z, pk(0x1.45f306p-1f), pk(12582912.0f));
   const float2 q = pk_add(t, pk(-12582912.0f));
   float2 r = pk_fma(q, pk(-0x1.921fb0p+00f), z);
@@ -91,13 +91,19 @@ __device__ __forceinline__ float2 pk_np_sin(float2 z) {
   s = pk_fma(s, r2, pk(-0x1.555556p-03f));
   s = pk_fma(s, r2, pk(0.0f));
   s = pk_fma(s, r, r);
-  // low two bits of t = quadrant mod 4 (see np_sincosf)
-  const uint32_t qx = __float_as_uint(t.x), qy = __float_as_uint(t.y);
+  // low two bits of t = quadrant mod 4 (see np_sincosf); cosine shifts it by one
+  const uint32_t qx = __float_as_uint(t.x) + (COS ? 1u : 0u), qy = __float_as_uint(t.y) + (COS ? 1u : 0u);
   float2 v = make_float2((qx & 1u) ? c.x : s.x, (qy & 1u) ? c.y : s.y);
   if (SQUARE) return pk_mul(v, v);
   if (qx & 2u) v.x = BT_SUB(0.0f, v.x);
   if (qy & 2u) v.y = BT_SUB(0.0f, v.y);
   return v;
+}
+
+// sin of both lanes (see pk_np_sincos)
+template <bool SQUARE, bool CHECKED = true>
+__device__ __forceinline__ float2 pk_np_sin(float2 z) {
+  return pk_np_sincos<false, SQUARE, CHECKED>(z);
 }
 
 }  // namespace bt
