@@ -323,6 +323,7 @@ def run_b200(args):
     from bt_b200.decoder import (FusedDecoder, build_stream, fill_conv_standins, host_inputs,
                                  stream_algorithmic_bytes, stream_launches)
     from bt_b200.runtime import BtRuntime
+    from bt_b200 import shard
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -346,24 +347,20 @@ def run_b200(args):
 
     S = build_stream(args.batch, t0=args.t0)
     dec = FusedDecoder(S, dev)
-    fill_conv_standins(dec, seed=17 + rank)
-    host = host_inputs(S, seed=100 + rank)
+    # rank r owns utterances shard.utterance_range(batch, r) of the job; its
+    # synthetic inputs are seeded per rank
+    fill_conv_standins(dec, seed=shard.rank_seed(17, rank))
+    host = host_inputs(S, seed=shard.rank_seed(100, rank))
     hin, hout = dec.host_buffers()
     dec.fill_host(hin, host)
     dec.run_host(hin, hout)             # inputs resident from here on
     torch.cuda.synchronize()
 
     def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+        shard.barrier(dev)
 
     def max_over_ranks(v):
-        if world > 1:
-            t = torch.tensor([v], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t.item())
-        return v
+        return shard.max_over_ranks(v, device=dev)
 
     for _ in range(args.warmup):
         dec.launch()
@@ -399,7 +396,7 @@ def run_b200(args):
             ad_n += 1
     achieved = ad_bytes / ad_time / 1e9
     traffic = read_profile_traffic()
-    roofline = {"bound": "hbm", "kernel": "bt_adain_snake (adain_snake_kernel)", "achieved": round(achieved, 1),
+    roofline = {"bound": "hbm", "kernel": "bt_adain_snake (adain_cluster_kernel)", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "frac_of_8TBps": round(achieved / NOMINAL_HBM, 4), "peak_kind": peak_kind,
                 "traffic": traffic, "launches_timed": ad_n,

@@ -163,3 +163,65 @@ def test_fused_chain_validates_then_reports_withdrawn(lib):
     prog.instr[0] = _lib.BtChainInstr(0, 1, 0, 0, 0.0)
     assert lib.bt_fused_chain(ctypes.byref(prog), (_lib.BtTensor * 1)(x), ctypes.byref(x)) == -5
     assert b"withdrawn" in lib.bt_last_error()
+
+
+@pytest.mark.gpu
+def test_ctypes_binding_without_torch_tensors():
+    """The INTEGRATION.md recipe: device memory from the CUDA runtime through
+    ctypes, one broadcast Add through bt_elementwise, numpy's bits back."""
+    import ctypes
+    import os
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    cudart = None
+    for name in ("/usr/local/cuda/lib64/libcudart.so", "libcudart.so", "libcudart.so.12"):
+        try:
+            cudart = ctypes.CDLL(name)
+            break
+        except OSError:
+            continue
+    if cudart is None:
+        pytest.skip("no libcudart to load by name")
+
+    class BtTensor(ctypes.Structure):
+        _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("rank", ctypes.c_int32),
+                    ("shape", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8)]
+
+    class BtEwAttrs(ctypes.Structure):
+        _fields_ = [("compute_dtype", ctypes.c_int32), ("alpha", ctypes.c_float)]
+
+    lib.bt_elementwise.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(BtTensor),
+                                   ctypes.POINTER(BtTensor), ctypes.POINTER(BtEwAttrs)]
+    lib.bt_last_error.restype = ctypes.c_char_p
+    ptrs = []
+
+    def device_copy(a):
+        p = ctypes.c_void_p()
+        assert cudart.cudaMalloc(ctypes.byref(p), ctypes.c_size_t(a.nbytes)) == 0
+        ptrs.append(p)
+        assert cudart.cudaMemcpy(p, a.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(a.nbytes), 1) == 0
+        return p
+
+    def view(p, shape, strides):
+        t = BtTensor()
+        t.data, t.dtype, t.rank = p, 10, len(shape)
+        for i, (n, s) in enumerate(zip(shape, strides)):
+            t.shape[i], t.strides[i] = n, s
+        return t
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((512, 1024), dtype=np.float32)
+    b = rng.standard_normal((512, 1), dtype=np.float32)
+    try:
+        dx, db, dy = device_copy(x), device_copy(b), device_copy(np.zeros_like(x))
+        ins = (BtTensor * 2)(view(dx, (512, 1024), (1024, 1)), view(db, (512, 1024), (1, 0)))
+        out = view(dy, (512, 1024), (1024, 1))
+        assert lib.bt_init(0) == 0
+        rc = lib.bt_elementwise(0, 2, ins, ctypes.byref(out), ctypes.byref(BtEwAttrs(10, 0.0)))
+        assert rc == 0, lib.bt_last_error()
+        assert lib.bt_sync() == 0
+        y = np.empty_like(x)
+        assert cudart.cudaMemcpy(y.ctypes.data_as(ctypes.c_void_p), dy, ctypes.c_size_t(y.nbytes), 2) == 0
+        assert np.array_equal(y.view(np.uint32), (x + b).view(np.uint32))
+    finally:
+        for p in ptrs:
+            cudart.cudaFree(p)
