@@ -53,6 +53,7 @@ constexpr int kMaxT = 49152;
 //       | A's remainder len % 8 (25-27) | B's remainder (28-30)
 struct SlotPlan {
   int32_t T, D, cs;
+  int32_t perfect;                     // 1: every leaf at depth D (leaf i = heap id 2^D + i)
   int32_t rank_e[kMaxCluster + 1];
   int32_t rank_slot[kMaxCluster + 1];
   uint32_t inner[kMaxIds / 32];        // bit h: heap node h is an inner node
@@ -117,6 +118,58 @@ __device__ __forceinline__ void tree_combine(float* hs, const uint32_t* inner, i
       __syncwarp();
     }
   }
+}
+
+// Sum of K consecutive leaves p[0..K) in pairwise order: (p0+p1), (p2+p3),
+// ... then pairs of those, and so on.
+template <int K>
+__device__ __forceinline__ float lane_leaves(const float* p) {
+  float v[K];
+  if constexpr (K == 2) {
+    const float2 q = *reinterpret_cast<const float2*>(p);
+    v[0] = q.x; v[1] = q.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < K; i += 4) {
+      const float4 q = *reinterpret_cast<const float4*>(p + i);
+      v[i] = q.x; v[i + 1] = q.y; v[i + 2] = q.z; v[i + 3] = q.w;
+    }
+  }
+#pragma unroll
+  for (int w = K; w > 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w / 2; ++i) v[i] = BT_ADD(v[2 * i], v[2 * i + 1]);
+  }
+  return v[0];
+}
+
+// Root of the pairwise tree held in hs (call from all 32 lanes of warp 0;
+// every lane returns it).  A perfect tree (every leaf at depth D, leaf i at
+// heap id 2^D + i) is summed with the same additions as tree_combine but in
+// registers: lane l adds its 2^D / 32 consecutive leaves pairwise, then xor
+// shuffles join sibling lanes level by level (float addition commutes).
+// Other trees go level by level through shared memory.
+__device__ __forceinline__ float tree_total(float* hs, const uint32_t* inner, int D, bool perfect) {
+  const int lane = threadIdx.x & 31;
+  if (perfect && D <= 9) {
+    const float* leaf = hs + (1 << D);
+    float v;
+    int levels = 5;
+    switch (D) {
+      case 9: v = lane_leaves<16>(leaf + 16 * lane); break;
+      case 8: v = lane_leaves<8>(leaf + 8 * lane); break;
+      case 7: v = lane_leaves<4>(leaf + 4 * lane); break;
+      case 6: v = lane_leaves<2>(leaf + 2 * lane); break;
+      default:
+        v = lane < (1 << D) ? leaf[lane] : 0.0f;
+        levels = D;
+        break;
+    }
+    for (int m = 0; m < levels; ++m) v = BT_ADD(v, __shfl_xor_sync(0xffffffffu, v, 1 << m));
+    return v;
+  }
+  tree_combine(hs, inner, D);
+  return hs[1];
 }
 
 __device__ __forceinline__ float2 shfl_xor2(unsigned mask, float2 v, int m) {
@@ -213,7 +266,8 @@ template <int NSRC, bool SNAKE>
 __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float prm[BT_ADAIN_MAX_OUT][4];   // gain, shift, alpha, 1/alpha of this row
-  __shared__ double scal[2];                   // mean, 1/sd (double) of this row
+  __shared__ float s_mu;                       // mean of this row
+  __shared__ double s_rsd;                     // RN64(1 / sd) of this row
   __shared__ int in_range[BT_ADAIN_MAX_OUT];   // output k's sin arguments provably in range
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = A.P.cs;                 // 1, 2, 4 or 8
@@ -283,41 +337,46 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
     else __syncthreads();
   };
 
-  // ReduceMean(h)
+  // ReduceMean(h).  np.mean: RN32(RN64(sum) / T), computed as
+  // RN32(RN64(sum * RN64(1/T))) -- the same float (division by a per-row
+  // constant, see div_by).  Warp 0 sums the tree and derives the row
+  // scalars; every other warp waits at the CTA barrier.
   slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
   sync_sums();
-  tree_combine(hs1, inner, A.P.D);
-  // np.mean: RN32(RN64(sum) / T), computed as RN32(RN64(sum * RN64(1/T)))
-  // -- the same float (division by a per-row constant, see div_by)
-  if (threadIdx.x == 0) scal[0] = (double)div_by(BT_ADD(0.0f, hs1[1]), A.rT);
+  if (threadIdx.x < 32) {
+    const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
+    if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
+  }
   __syncthreads();
-  const float mu = (float)scal[0];
+  const float mu = s_mu;
   // Sub, Mul(d, d), ReduceMean, Add eps, Sqrt
   slot_pass<1, true>(sw, ns, b0, nullptr, nullptr, mu, hs2, cluster, cs);
   sync_sums();
-  tree_combine(hs2, inner, A.P.D);
-  if (threadIdx.x == 0) {
-    const float var = div_by(BT_ADD(0.0f, hs2[1]), A.rT);
-    const float sd = BT_SQRT(BT_ADD(var, A.eps));
-    const double rsd0 = recip_d(sd);
-    scal[1] = rsd0;
-    if (SNAKE) {
-      // Every |h_i - mu|^2 is at most S = sum_j (h_j - mu)^2, whose float32
-      // pairwise sum S' has a relative error far below 2^-10; the normalised
-      // value, the affine step and the alpha product each add one rounding
-      // (factors 1 + 2^-20 below cover them).  When the bound on |alpha * y|
-      // is under half numpy's reduction range, no argument can leave it
-      // (NaN or Inf anywhere makes the bound fail and keeps the checks).
-      const double nb = sqrt((double)hs2[1] * (1.0 + 0x1p-10)) * rsd0 * (1.0 + 0x1p-20);
-      for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
-        const double zb = fabs((double)prm[k][2]) *
-                          (fabs((double)prm[k][0]) * nb + fabs((double)prm[k][1])) * (1.0 + 0x1p-20);
-        in_range[k] = (k < A.n_out && zb <= 0.5 * 117435.992) ? 1 : 0;
+  if (threadIdx.x < 32) {
+    const float ssq = tree_total(hs2, inner, A.P.D, A.P.perfect != 0);
+    if (threadIdx.x == 0) {
+      const float var = div_by(BT_ADD(0.0f, ssq), A.rT);
+      const float sd = BT_SQRT(BT_ADD(var, A.eps));
+      const double rsd0 = recip_d(sd);
+      s_rsd = rsd0;
+      if (SNAKE) {
+        // Every |h_i - mu| is at most sqrt(S), S = sum_j (h_j - mu)^2, so
+        // |n_i| <= sqrt(S) / sd; the float32 sum of S and each later
+        // rounding are far inside the 1 % margins below.  When the bound on
+        // |alpha * y| is under half numpy's reduction range, no argument can
+        // leave it (NaN or Inf anywhere makes the comparison false and keeps
+        // the checks).
+        const float nb = BT_MUL(BT_MUL(BT_SQRT(ssq), (float)rsd0), 1.01f);
+        for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
+          const float zb = BT_MUL(BT_MUL(fabsf(prm[k][2]), BT_ADD(BT_MUL(fabsf(prm[k][0]), nb), fabsf(prm[k][1]))),
+                                  1.01f);
+          in_range[k] = (k < A.n_out && zb <= 0.5f * 117435.992f) ? 1 : 0;
+        }
       }
     }
   }
   __syncthreads();
-  const double rsd = scal[1];
+  const double rsd = s_rsd;
 
   // residual h and the outputs of this segment (coalesced, 128-bit where the
   // phases agree)
@@ -449,6 +508,7 @@ const ClusterPlan& cluster_plan(int T, int cs) {
   cp.P.T = T;
   cp.P.D = hp.D;
   cp.P.cs = cs;
+  cp.P.perfect = ((int64_t)hp.off.size() == (1ll << hp.D)) ? 1 : 0;
   for (int i = 0; i < kMaxIds / 32; ++i) cp.P.inner[i] = hp.inner[i];
   std::vector<int> first;
   bool ok = rank_split(hp, cs, first) && (2 << hp.D) <= kMaxIds;
