@@ -293,17 +293,6 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   for (int i = threadIdx.x; i < kMaxIds / 32; i += kThreads) inner[i] = A.P.inner[i];
   const int bt = A.log2_c >= 0 ? (row32 >> A.log2_c) : row32 / A.channels32;
   const int c = row32 - bt * A.channels32;
-#pragma unroll
-  for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
-    if (threadIdx.x == 32 * k && k < A.n_out) {
-      prm[k][0] = A.gain[k][bt * A.gain_stride + c];
-      prm[k][1] = A.shift[k][bt * A.shift_stride + c];
-      if (SNAKE) {
-        prm[k][2] = ldf(A.alpha[k], A.alpha_dtype, c);
-        prm[k][3] = ldf(A.inv_alpha[k], A.alpha_dtype, c);
-      }
-    }
-  }
   // sources from the next 16-byte boundary; indexing smem directly (no
   // integer round trip) keeps the pointers in the shared address space
   const int sb_words = (2 * ids + 2 * ns + kMaxIds / 32 + 3) & ~3;
@@ -319,6 +308,19 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   stage_async(b0, g0, seg);
   if (NSRC > 1) stage_async(b1, g1, seg);
   if (NSRC > 2) stage_async(b2, g2, seg);
+  // the row constants after the copies are issued: their loads overlap the
+  // copies instead of delaying them
+#pragma unroll
+  for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
+    if (threadIdx.x == 32 * k && k < A.n_out) {
+      prm[k][0] = A.gain[k][bt * A.gain_stride + c];
+      prm[k][1] = A.shift[k][bt * A.shift_stride + c];
+      if (SNAKE) {
+        prm[k][2] = ldf(A.alpha[k], A.alpha_dtype, c);
+        prm[k][3] = ldf(A.inv_alpha[k], A.alpha_dtype, c);
+      }
+    }
+  }
   cp_async_wait_all();
   // A CTA barrier for the staged rows, the plan and the row constants; with
   // cs > 1 also the guarantee that every CTA of the cluster runs before any
@@ -343,9 +345,25 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   // scalars; every other warp waits at the CTA barrier.
   slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
   sync_sums();
+  int head = (4 - phase4(g0)) & 3;
+  if (head > seg) head = seg;
+  const int nvec = (seg - head) >> 2;
   if (threadIdx.x < 32) {
     const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
+  } else if (A.res) {
+    // the residual h is complete after the first pass: warps 1.. write it
+    // while warp 0 sums the tree (128-bit where the phases agree)
+    const int t = (int)threadIdx.x - 32;
+    constexpr int kW = kThreads - 32;
+    float* r = A.res + gofs;
+    if (phase4(r) == phase4(g0)) {
+      for (int q = t; q < nvec; q += kW) __stcs((float4*)(r + head + 4 * q), *(const float4*)(b0 + head + 4 * q));
+      for (int i = t; i < head; i += kW) r[i] = b0[i];
+      for (int i = head + 4 * nvec + t; i < seg; i += kW) r[i] = b0[i];
+    } else {
+      for (int i = t; i < seg; i += kW) r[i] = b0[i];
+    }
   }
   __syncthreads();
   const float mu = s_mu;
@@ -378,22 +396,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   __syncthreads();
   const double rsd = s_rsd;
 
-  // residual h and the outputs of this segment (coalesced, 128-bit where the
-  // phases agree)
-  int head = (4 - phase4(g0)) & 3;
-  if (head > seg) head = seg;
-  const int nvec = (seg - head) >> 2;
-  if (A.res) {
-    float* r = A.res + gofs;
-    if (phase4(r) == phase4(g0)) {
-      for (int q = threadIdx.x; q < nvec; q += kThreads)
-        __stcs((float4*)(r + head + 4 * q), *(const float4*)(b0 + head + 4 * q));
-      for (int i = threadIdx.x; i < head; i += kThreads) r[i] = b0[i];
-      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
-    } else {
-      for (int i = threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
-    }
-  }
+  // the outputs of this segment (coalesced, 128-bit where the phases agree)
   const float2 nmu = pk(-mu);
 #pragma unroll
   for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
