@@ -285,7 +285,8 @@ def per_op(rt, torch, peak):
                                                      ("Mul", ["d", "gain"], ["y"], {})], dict(c)))
     c = configs.c4_cast()
     Xc = dev(c["X"])
-    entry("c4_cast", lambda: rt.elementwise("IDENTITY", [Xc], Xc.shape, np.float32, np.float64), 492000000,
+    entry("c4_cast", lambda: rt.elementwise("IDENTITY", [Xc], Xc.shape, np.float32,
+                                            rt._cast_compute(np.float16, np.float32)), 492000000,
           onode("Cast", c, ["X"], {"to": 1}))
     del Xc
     # >= 256 MB sweep

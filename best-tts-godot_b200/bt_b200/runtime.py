@@ -142,7 +142,7 @@ class BtRuntime:
     def _widen(self, t):
         """fp16 tensor -> fp32 copy (kernel), other dtypes unchanged."""
         if t.dtype == torch.float16:
-            return self.elementwise("IDENTITY", [t], t.shape, np.float32, np.float64)
+            return self.elementwise("IDENTITY", [t], t.shape, np.float32, np.float32)
         return t
 
     def _contig(self, t):
@@ -327,6 +327,10 @@ class BtRuntime:
             return np.dtype(np.int64)
         if src.kind in "iub" and dst.kind == "f":
             return np.dtype(np.int64)
+        if src.kind == "f" and dst == np.float32:
+            # float16 widens exactly and float64 rounds once (the load's
+            # conversion) -- the same float32 as numpy's astype
+            return np.dtype(np.float32)
         return np.dtype(np.float64)
 
     def _cast_compute_where(self, dt):

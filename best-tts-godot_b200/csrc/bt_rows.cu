@@ -24,6 +24,10 @@
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
+#include "bt_async.h"
+#include <map>
+#include <mutex>
+#include <vector>
 
 namespace bt {
 namespace {
@@ -198,7 +202,6 @@ __device__ float block_max(const float* s, int n, float* red) {
 }
 
 // ---- row staging --------------------------------------------------------------
-__device__ __forceinline__ int phase4(const void* p) { return (int)(((uintptr_t)p >> 2) & 3); }
 
 // First element index at which g is 16-byte aligned, and the number of
 // 4-element vectors after it.
@@ -591,6 +594,345 @@ int row_grid(int64_t rows) {
   return (int)g;
 }
 
+// ---- warp-per-row kernels --------------------------------------------------
+// Rows of at most kWarpRowMax values (softmax over 510 keys, layer norm over
+// 768 channels, means over 2048 frames) are too short to keep a CTA busy:
+// here one warp owns a row end to end.  It stages the row into its own slice
+// of shared memory with cp.async, sums numpy's pairwise tree from a plan the
+// host built once per row length (four groups of eight lanes, one leaf per
+// group at a time, lane j holding numpy's accumulator j), combines the tree
+// in registers (perfect trees) or level by level, and writes the outputs.
+// Only warp-level synchronisation; eight independent rows per CTA.
+constexpr int kWarpRowMax = 2048;   // -> at most 32 leaves, depth <= 5
+constexpr int kWarpLeaves = 32;
+constexpr int kWarpHeap = 64;       // heap ids < 2^(D+1) <= 64
+constexpr int kWarpsPerCta = 8;
+
+struct WPlan {
+  int32_t n, D, n_leaf, perfect;     // perfect: every leaf at depth D
+  uint32_t inner[2];                 // bit h: heap node h is an inner node
+  uint16_t off[kWarpLeaves];         // leaf offsets, in row order
+  uint8_t len[kWarpLeaves];          // leaf lengths (<= 128)
+  uint8_t id[kWarpLeaves];           // heap ids (< 64)
+};
+
+// The plan as the kernels read it: copied once per CTA into shared memory
+// (lane-divergent reads of a kernel parameter array would be serialised).
+struct WView {
+  const uint16_t* off;
+  const uint8_t* len;
+  const uint8_t* id;
+  const uint32_t* inner;
+  int n, D, n_leaf, perfect;
+};
+struct WShared {
+  uint16_t off[kWarpLeaves];
+  uint8_t len[kWarpLeaves];
+  uint8_t id[kWarpLeaves];
+  uint32_t inner[2];
+};
+__device__ __forceinline__ WView wplan_load(const WPlan& P, WShared& sh) {
+  for (int i = threadIdx.x; i < P.n_leaf; i += blockDim.x) {
+    sh.off[i] = P.off[i];
+    sh.len[i] = P.len[i];
+    sh.id[i] = P.id[i];
+  }
+  if (threadIdx.x < 2) sh.inner[threadIdx.x] = P.inner[threadIdx.x];
+  __syncthreads();
+  WView v;
+  v.off = sh.off; v.len = sh.len; v.id = sh.id; v.inner = sh.inner;
+  v.n = P.n; v.D = P.D; v.n_leaf = P.n_leaf; v.perfect = P.perfect;
+  return v;
+}
+
+// Floats of one warp's shared slice: the heap, then the row (+ 4 for the
+// 16-byte phase), rounded to 16 bytes.
+__host__ __device__ inline int wrow_stride(int n) { return kWarpHeap + (((n + 4) + 3) & ~3); }
+
+// numpy's pairwise sum of f(row[i]) over the whole row (all 32 lanes call;
+// every lane returns the sum, before numpy's "+ 0.0").
+template <class F>
+__device__ __forceinline__ float warp_pw_sum(const WView& P, const float* row, float* heap, F f) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane & 7, g = lane >> 3;
+  const unsigned gmask = 0xffu << (lane & 24);
+  for (int L = g; L < P.n_leaf; L += 4) {
+    const int off = P.off[L], len = P.len[L];
+    const int steps = len >> 3, end = steps << 3;
+    const float* q = row + off + j;
+    float acc = -0.0f;                      // -0.0 + x == x: acc starts as numpy's r[j] = a[j]
+#pragma unroll 4
+    for (int m = 0; m < steps; ++m) acc = BT_ADD(acc, f(q[8 * m]));
+    // numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); addition commutes
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 1));
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 2));
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 4));
+    if (steps == 0) acc = 0.0f;             // a run shorter than 8 is summed from +0.0
+    if (len > end) {
+      if (j == 0)
+        for (int i = end; i < len; ++i) acc = BT_ADD(acc, f(row[off + i]));
+      acc = __shfl_sync(gmask, acc, 0, 8);
+    }
+    if (j == 0) heap[P.id[L]] = acc;
+  }
+  __syncwarp();
+  float total;
+  if (P.perfect) {
+    const int nl = 1 << P.D;                // leaf i sits at heap id nl + i
+    total = lane < nl ? heap[nl + lane] : 0.0f;
+    for (int m = 1; m < nl; m <<= 1) total = BT_ADD(total, __shfl_xor_sync(0xffffffffu, total, m));
+    // with fewer than 32 leaves only lanes < nl hold the root: share lane 0's
+    total = __shfl_sync(0xffffffffu, total, 0);
+  } else {
+    for (int k = P.D - 1; k >= 0; --k) {
+      for (int jj = lane; jj < (1 << k); jj += 32) {
+        const int h = (1 << k) + jj;
+        if ((P.inner[h >> 5] >> (h & 31)) & 1u) heap[h] = BT_ADD(heap[2 * h], heap[2 * h + 1]);
+      }
+      __syncwarp();
+    }
+    total = heap[1];
+  }
+  __syncwarp();                             // the heap is reused by the next sum
+  return total;
+}
+
+struct WReduceArgs {
+  WPlan P;
+  const void* x;
+  int32_t xdt, mean;
+  int64_t rows;
+  float* out;
+};
+struct WSoftmaxArgs {
+  WPlan P;
+  SoftmaxArgs a;
+};
+struct WLayerNormArgs {
+  WPlan P;
+  LayerNormArgs a;
+};
+
+// This warp's heap and row slice; the row buffer shares g's 16-byte phase.
+struct WSlice {
+  float* heap;
+  float* slice;
+};
+__device__ __forceinline__ WSlice warp_slice(unsigned char* smem, int n) {
+  WSlice w;
+  w.heap = reinterpret_cast<float*>(smem) + (threadIdx.x >> 5) * wrow_stride(n);
+  w.slice = w.heap + kWarpHeap;
+  return w;
+}
+
+// Calls body(row, b) for this warp's rows (one per warp on a full grid, more
+// when the grid is smaller) with b = the staged copy of src(row).
+template <class Src, class Body>
+__device__ __forceinline__ void warp_rows(const WSlice& W, int n, int64_t rows, Src src, Body body) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    const float* g = src(row);
+    float* b = W.slice + phase4(g);
+    stage_floats_async(b, g, n, lane, 32);
+    cp_async_wait_all();
+    __syncwarp();
+    body(row, b);
+    __syncwarp();   // the slice is reused by this warp's next row
+  }
+}
+
+__global__ void __launch_bounds__(256) wrow_reduce_kernel(WReduceArgs A) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ WShared sh;
+  const WView P = wplan_load(A.P, sh);
+  const int lane = threadIdx.x & 31, n = P.n;
+  const WSlice W = warp_slice(smem, n);
+  auto finish = [&](int64_t row, const float* b) {
+    const float sum = BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwIdentity()));
+    if (lane == 0) A.out[row] = A.mean ? np_mean_from_sum(sum, n) : sum;
+  };
+  if (A.xdt == BT_F32) {
+    const float* x = (const float*)A.x;
+    warp_rows(W, n, A.rows, [&](int64_t row) { return x + row * n; }, finish);
+    return;
+  }
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < A.rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    const __half* g = (const __half*)A.x + row * n;
+    for (int i = lane; i < n; i += 32) W.slice[i] = __half2float(g[i]);
+    __syncwarp();
+    finish(row, W.slice);
+    __syncwarp();
+  }
+}
+
+// Writes o[i] = f(b[i]) for the row, 128-bit where o shares g's phase.
+template <class F>
+__device__ __forceinline__ void warp_write(float* o, const float* b, const float* g, int n, F f) {
+  const int lane = threadIdx.x & 31;
+  if (phase4(o) == phase4(g)) {
+    int head = (4 - phase4(o)) & 3;
+    if (head > n) head = n;
+    const int nvec = (n - head) >> 2;
+    for (int i = lane; i < head; i += 32) o[i] = f(b[i], i);
+    for (int q = lane; q < nvec; q += 32) {
+      const int i = head + 4 * q;
+      const float4 v = *reinterpret_cast<const float4*>(b + i);
+      __stcs(reinterpret_cast<float4*>(o + i), make_float4(f(v.x, i), f(v.y, i + 1), f(v.z, i + 2), f(v.w, i + 3)));
+    }
+    for (int i = head + 4 * nvec + lane; i < n; i += 32) o[i] = f(b[i], i);
+  } else {
+    for (int i = lane; i < n; i += 32) o[i] = f(b[i], i);
+  }
+}
+
+__global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ WShared sh;
+  const WView P = wplan_load(A.P, sh);
+  const SoftmaxArgs& a = A.a;
+  const int lane = threadIdx.x & 31, n = P.n;
+  const WSlice W = warp_slice(smem, n);
+  const float* x = a.x;
+  warp_rows(W, n, a.rows, [&](int64_t row) { return x + row * (int64_t)n; }, [&](int64_t row, float* b) {
+    if (a.mask) {
+      int64_t rem = row, moff = 0;
+      for (int d = a.lead_rank - 1; d >= 0; --d) {
+        const int64_t c = rem % a.lead_shape[d];
+        rem /= a.lead_shape[d];
+        moff += c * a.mask_lead_st[d];
+      }
+      for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], a.mask[moff + i * a.mask_col_st]);
+    }
+    // np.max (NaN propagates)
+    float m = -INFINITY;
+    bool nan = false;
+    for (int i = lane; i < n; i += 32) {
+      const float v = b[i];
+      if (v != v) nan = true;
+      m = fmaxf(m, v);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
+    }
+    if (nan) m = qnan();
+    for (int i = lane; i < n; i += 32) b[i] = np_expf(BT_SUB(b[i], m));
+    __syncwarp();
+    const float denom = BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwIdentity()));
+    const double rd = recip_d(denom);
+    warp_write(a.out + row * (int64_t)n, b, x + row * (int64_t)n, n, [=](float v, int) { return div_by(v, rd); });
+  });
+}
+
+__global__ void __launch_bounds__(256) wrow_layernorm_kernel(WLayerNormArgs A) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ WShared sh;
+  const WView P = wplan_load(A.P, sh);
+  const LayerNormArgs& a = A.a;
+  const int lane = threadIdx.x & 31, n = P.n;
+  const WSlice W = warp_slice(smem, n);
+  const float* x = a.x;
+  warp_rows(W, n, a.rows, [&](int64_t row) { return x + row * (int64_t)n; }, [&](int64_t row, float* b) {
+    if (a.skip || a.bias) {
+      const float* sk = a.skip ? a.skip + row * (int64_t)n : nullptr;
+      for (int i = lane; i < n; i += 32) {
+        float v = b[i];
+        if (sk) v = BT_ADD(v, sk[i]);
+        if (a.bias) v = BT_ADD(v, a.bias[i]);
+        b[i] = v;
+      }
+      __syncwarp();
+    }
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwIdentity())), n);
+    const float var = np_mean_from_sum(BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwSquaredDev{mu})), n);
+    const float sd = BT_SQRT(BT_ADD(var, a.eps));
+    const double rsd = recip_d(sd);
+    float* o = a.out + row * (int64_t)n;
+    for (int i = lane; i < n; i += 32) {
+      float y = BT_MUL(div_by(BT_SUB(b[i], mu), rsd), ldf(a.gamma, a.gdt, i));
+      if (a.beta) y = BT_ADD(y, ldf(a.beta, a.bdt, i));
+      o[i] = y;
+    }
+  });
+}
+
+// ---- warp-row host side ------------------------------------------------------
+void wplan_node(WPlan& p, int h, int lo, int n, bool& ok) {
+  if (n <= kPwLeaf) {
+    if (p.n_leaf >= kWarpLeaves || h >= kWarpHeap) { ok = false; return; }
+    p.off[p.n_leaf] = (uint16_t)lo;
+    p.len[p.n_leaf] = (uint8_t)n;
+    p.id[p.n_leaf] = (uint8_t)h;
+    ++p.n_leaf;
+    return;
+  }
+  if (h >= kWarpHeap) { ok = false; return; }
+  p.inner[h >> 5] |= 1u << (h & 31);
+  const int n2 = (int)pw_split(n);
+  wplan_node(p, 2 * h, lo, n2, ok);
+  wplan_node(p, 2 * h + 1, lo + n2, n - n2, ok);
+}
+
+// The pairwise plan of a row of n values for the warp kernels (cached per
+// n); false when n is outside their cover.
+bool wplan_for(int n, WPlan* out) {
+  if (n < 1 || n > kWarpRowMax) return false;
+  static std::mutex mu;
+  static std::map<int, WPlan> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(n);
+  if (it == cache.end()) {
+    WPlan p;
+    memset(&p, 0, sizeof(p));
+    p.n = n;
+    p.D = pw_depth(n);
+    bool ok = p.D <= 5;
+    if (ok) wplan_node(p, 1, 0, n, ok);
+    p.perfect = (ok && p.n_leaf == (1 << p.D)) ? 1 : 0;
+    if (!ok) p.n = -1;
+    it = cache.emplace(n, p).first;
+  }
+  if (it->second.n < 0) return false;
+  *out = it->second;
+  return true;
+}
+
+std::atomic<int> g_wrow_ready[kMaxDevices];
+
+// Launch geometry of a warp-row kernel: its dynamic shared memory (eight
+// slices) and one warp per row.  (A persistent grid with the next row's copy
+// in flight measured slower: the second buffer halves the warps per SM.)
+// Returns BT_EUNSUPPORTED, without setting an error, when there are too few
+// rows to fill the device one warp per row (the CTA-per-row kernels serve
+// those).
+int wrow_setup(int n, int64_t rows, size_t* smem, int* grid) {
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  if (di.device >= kMaxDevices) return set_error(BT_EUNSUPPORTED, "device ordinal %d >= %d", di.device, kMaxDevices);
+  if (rows < 2ll * di.sm_count * kWarpsPerCta) return BT_EUNSUPPORTED;
+  if (!g_wrow_ready[di.device].load()) {
+    const void* fns[] = {(const void*)wrow_reduce_kernel, (const void*)wrow_softmax_kernel,
+                         (const void*)wrow_layernorm_kernel};
+    for (const void* f : fns) {
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, f);
+      if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+      e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               di.max_smem_optin - (int)fa.sharedSizeBytes);
+      if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
+    g_wrow_ready[di.device].store(1);
+  }
+  *smem = (size_t)kWarpsPerCta * wrow_stride(n) * sizeof(float);
+  int64_t g = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+  if (g > 2147483647) g = 2147483647;
+  *grid = (int)g;
+  return BT_OK;
+}
+
 }  // namespace
 }  // namespace bt
 
@@ -650,6 +992,18 @@ extern "C" int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int 
   }
   cudaStream_t s = cur_stream();
   if (I == 1) {
+    WPlan wp;
+    if (R <= kWarpRowMax && wplan_for((int)R, &wp)) {
+      size_t smem;
+      int grid;
+      rc = wrow_setup((int)R, O, &smem, &grid);
+      if (rc == BT_OK) {
+        WReduceArgs a{wp, x->data, x->dtype, kind == BT_REDUCE_MEAN, O, (float*)out->data};
+        wrow_reduce_kernel<<<grid, 32 * kWarpsPerCta, smem, s>>>(a);
+        return check_launch("bt_reduce(warp rows)");
+      }
+      if (rc != BT_EUNSUPPORTED) return rc;
+    }
     if (R > kMaxRow) return set_error(BT_ETOOBIG, "bt_reduce: reduced run of %lld values exceeds %d", (long long)R, kMaxRow);
     size_t smem;
     int depth;
@@ -700,6 +1054,18 @@ extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, c
       else a.mask_col_st = st;
     }
     a.mask = (const float*)mask->data;
+  }
+  WPlan wp;
+  if (n <= kWarpRowMax && wplan_for((int)n, &wp)) {
+    size_t smem;
+    int grid;
+    rc = wrow_setup((int)n, rows, &smem, &grid);
+    if (rc == BT_OK) {
+      WSoftmaxArgs w{wp, a};
+      wrow_softmax_kernel<<<grid, 32 * kWarpsPerCta, smem, cur_stream()>>>(w);
+      return check_launch("bt_softmax(warp rows)");
+    }
+    if (rc != BT_EUNSUPPORTED) return rc;
   }
   size_t smem;
   int depth;
@@ -757,6 +1123,18 @@ extern "C" int bt_layernorm(const bt_tensor* x, const bt_tensor* skip, const bt_
   a.rows = rows;
   a.eps = eps;
   a.out = (float*)out->data;
+  WPlan wp;
+  if (n <= kWarpRowMax && wplan_for((int)n, &wp)) {
+    size_t smem;
+    int grid;
+    rc = wrow_setup((int)n, rows, &smem, &grid);
+    if (rc == BT_OK) {
+      WLayerNormArgs w{wp, a};
+      wrow_layernorm_kernel<<<grid, 32 * kWarpsPerCta, smem, cur_stream()>>>(w);
+      return check_launch("bt_layernorm(warp rows)");
+    }
+    if (rc != BT_EUNSUPPORTED) return rc;
+  }
   size_t smem;
   int depth;
   if (n > kMaxRow) return set_error(BT_ETOOBIG, "bt_layernorm: normalised run of %lld values exceeds %d", (long long)n, kMaxRow);
