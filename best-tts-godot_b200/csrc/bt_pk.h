@@ -100,6 +100,40 @@ __device__ __forceinline__ float2 pk_np_sincos(float2 z) {
   return v;
 }
 
+// Both lanes through the scalar np_expf (NaN and the saturated ranges; the
+// scalar function is short, so it stays inline -- no call, no stack frame).
+__device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_expf(x.x), np_expf(x.y)); }
+
+// exp of both lanes, np_expf step for step.  The quadrant k = (int)q is read
+// from the bits of t = RN(RN(x * log2e) + 1.5*2^23): t lies in [2^23, 2^24)
+// with ulp 1, so t's bits minus those of 1.5*2^23 are q, negatives included.
+__device__ __forceinline__ float2 pk_np_exp(float2 x) {
+  const float kXmax = 88.72283935546875f;
+  const float kXmin = -103.97208404541015625f;
+  // NaN fails every comparison and takes the scalar path, like the ranges
+  if (!(x.x < kXmax && x.x > kXmin && x.y < kXmax && x.y > kXmin)) return pk_exp_edge(x);
+  const float kMagic = 12582912.0f;   // 1.5 * 2^23
+  // product then sum: lane by lane (two roundings, see pk_add_lanes)
+  const float2 t = pk_add_lanes(pk_mul(x, pk(1.442695040888963407359924681001892137f)), pk(kMagic));
+  const float2 q = pk_add(t, pk(-kMagic));
+  float2 r = pk_fma(q, pk(-6.93145752e-1f), x);
+  r = pk_fma(q, pk(-1.42860677e-6f), r);
+  float2 num = pk_fma(pk(5.082762527590693718096e-04f), r, pk(6.757896990527504603057e-03f));
+  num = pk_fma(num, r, pk(5.114512081637298353406e-02f));
+  num = pk_fma(num, r, pk(2.473615434895520810817e-01f));
+  num = pk_fma(num, r, pk(7.257664613233124478488e-01f));
+  num = pk_fma(num, r, pk(9.999999999980870924916e-01f));
+  float2 den = pk_fma(pk(2.159509375685829852307e-02f), r, pk(-2.742335390411667452936e-01f));
+  den = pk_fma(den, r, pk(1.0f));
+  const float2 pq = make_float2(BT_DIV(num.x, den.x), BT_DIV(num.y, den.y));
+  // scale_pow2(pq, k): two exact-power multiplies
+  const int kx = (int)(__float_as_uint(t.x) - 0x4B400000u), ky = (int)(__float_as_uint(t.y) - 0x4B400000u);
+  const int kx1 = kx / 2, ky1 = ky / 2;
+  const float2 s1 = make_float2(pow2i(kx1), pow2i(ky1));
+  const float2 s2 = make_float2(pow2i(kx - kx1), pow2i(ky - ky1));
+  return pk_mul(pk_mul(pq, s1), s2);
+}
+
 // sin of both lanes (see pk_np_sincos)
 template <bool SQUARE, bool CHECKED = true>
 __device__ __forceinline__ float2 pk_np_sin(float2 z) {

@@ -25,6 +25,7 @@
 #include "bt_internal.h"
 #include "bt_core.h"
 #include "bt_async.h"
+#include "bt_pk.h"
 #include <map>
 #include <mutex>
 #include <vector>
@@ -342,6 +343,7 @@ struct SoftmaxArgs {
   int64_t lead_shape[BT_MAX_RANK];
   int64_t mask_lead_st[BT_MAX_RANK]; // mask stride per leading axis (0 = broadcast)
   int64_t mask_col_st;               // mask stride along the softmax axis (0 or 1)
+  int32_t mask_row_const;            // 1: every leading stride is 0 (one mask row for all rows)
   float* out;
 };
 
@@ -797,13 +799,27 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
   const float* x = a.x;
   warp_rows(W, n, a.rows, [&](int64_t row) { return x + row * (int64_t)n; }, [&](int64_t row, float* b) {
     if (a.mask) {
-      int64_t rem = row, moff = 0;
-      for (int d = a.lead_rank - 1; d >= 0; --d) {
-        const int64_t c = rem % a.lead_shape[d];
-        rem /= a.lead_shape[d];
-        moff += c * a.mask_lead_st[d];
+      // the mask row of this row: lane 0 unravels the row index (64-bit
+      // division) only when the mask varies along the leading axes
+      long long moff = 0;
+      if (!a.mask_row_const) {
+        if (lane == 0) {
+          int64_t rem = row;
+          for (int d = a.lead_rank - 1; d >= 0; --d) {
+            const int64_t c = rem % a.lead_shape[d];
+            rem /= a.lead_shape[d];
+            moff += c * a.mask_lead_st[d];
+          }
+        }
+        moff = __shfl_sync(0xffffffffu, moff, 0);
       }
-      for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], a.mask[moff + i * a.mask_col_st]);
+      const float* mr = a.mask + moff;
+      if (a.mask_col_st) {
+        for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], mr[i]);
+      } else {
+        const float mv = mr[0];
+        for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], mv);
+      }
     }
     // np.max (NaN propagates)
     float m = -INFINITY;
@@ -818,7 +834,14 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
       nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
     }
     if (nan) m = qnan();
-    for (int i = lane; i < n; i += 32) b[i] = np_expf(BT_SUB(b[i], m));
+    // exp(x - max), elements i and i + 32 two at a time (x - m == x + (-m))
+    int i = lane;
+    for (; i + 32 < n; i += 64) {
+      const float2 e = pk_np_exp(pk_add(pk(b[i], b[i + 32]), pk(-m)));
+      b[i] = e.x;
+      b[i + 32] = e.y;
+    }
+    if (i < n) b[i] = np_expf(BT_SUB(b[i], m));
     __syncwarp();
     const float denom = BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwIdentity()));
     const double rd = recip_d(denom);
@@ -1054,6 +1077,9 @@ extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, c
       else a.mask_col_st = st;
     }
     a.mask = (const float*)mask->data;
+    a.mask_row_const = 1;
+    for (int d = 0; d < a.lead_rank; ++d)
+      if (a.mask_lead_st[d] != 0) a.mask_row_const = 0;
   }
   WPlan wp;
   if (n <= kWarpRowMax && wplan_for((int)n, &wp)) {
