@@ -496,6 +496,38 @@ def run_profile_adain(args):
     return 0
 
 
+PROFILE_OPS = ("reducemean_c2", "softmax_c3_b16", "layernorm_768")
+
+
+def run_profile_op(args):
+    """One per-op workload, launched warmup + steps times, for ncu:
+    'reducemean_c2' (BASELINE c2 ReduceMean, [64,512,2048]), 'softmax_c3_b16'
+    (c3 masked softmax at batch 16) or 'layernorm_768' (LayerNormalization
+    over 768 channels of a 256 MB tensor)."""
+    import torch
+    from bt_b200 import configs
+    from bt_b200.runtime import BtRuntime
+    torch.cuda.set_device(0)
+    rt = BtRuntime(0)
+    name = args.profile_op
+    if name == "reducemean_c2":
+        X = torch.from_numpy(configs.c2_reducemean()["X"]).cuda()
+        fn = lambda: rt._reduce_block(X, [2], 1)
+    elif name == "softmax_c3_b16":
+        c = configs.c3(batch=16)
+        Xs, M = torch.from_numpy(c["X"]).cuda(), torch.from_numpy(c["mask"]).cuda()
+        fn = lambda: rt.softmax(Xs, M, -1)
+    else:
+        A = torch.randn((64 * 1024 * 1024 // 768, 768), device="cuda")
+        g = torch.rand(768, device="cuda")
+        fn = lambda: rt.layernorm(A, None, None, g, None, -1, 1e-5)
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_op": name, "launches": args.warmup + args.steps}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -511,9 +543,13 @@ def main():
                     help="run only stage-2 bt_adain_snake launches (for ncu)")
     ap.add_argument("--profile-kind", default="2src", choices=sorted(PROFILE_KINDS),
                     help="which bt_adain_snake launch --profile-adain runs")
+    ap.add_argument("--profile-op", default=None, choices=PROFILE_OPS,
+                    help="run only one per-op workload (for ncu)")
     args = ap.parse_args()
     if args.profile_adain:
         return run_profile_adain(args)
+    if args.profile_op:
+        return run_profile_op(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
