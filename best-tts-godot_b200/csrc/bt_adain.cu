@@ -89,8 +89,6 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
-__device__ __forceinline__ double recip_d(float b) { return __ddiv_rn(1.0, (double)b); }
-__device__ __forceinline__ float div_by(float a, double rb) { return __double2float_rn(__dmul_rn((double)a, rb)); }
 __device__ __forceinline__ float ldf(const void* p, int dt, int64_t i) {
   return dt == BT_F16 ? __half2float(((const __half*)p)[i]) : ((const float*)p)[i];
 }

@@ -73,6 +73,62 @@ BT_HD float scale_pow2(float p, int k) {
   return BT_MUL(BT_MUL(p, pow2i(k1)), pow2i(k2));
 }
 
+#if defined(__CUDACC__)
+// The hardware reciprocal approximation (rcp.approx.ftz.f32, relative error
+// within about 1 ulp; subnormal operands and results flush to zero).
+__device__ __forceinline__ float rcp_approx(float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  return y;
+}
+// RN(a / b) by Markstein's method: the reciprocal approximation refined by
+// one Newton-Raphson step, the quotient a*y corrected by one exact FMA
+// residual step (P. Markstein, "Computation of elementary functions on the
+// IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; Muller et
+// al., Handbook of Floating-Point Arithmetic, the chapter on FMA-based
+// division).  Only for operands whose reciprocal, quotient and residual stay
+// normal and finite -- every caller bounds its operands -- and every use is
+// checked bit for bit against IEEE division over all of its float32 inputs
+// (bt_selfcheck).
+__device__ __forceinline__ float div_nr(float a, float b) {
+  float y = rcp_approx(b);
+  const float e = __fmaf_rn(-b, y, 1.0f);
+  y = __fmaf_rn(y, e, y);
+  const float q = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-b, q, a);
+  return __fmaf_rn(r, y, q);
+}
+
+// 1 / b in double for a float b, within one double ulp of RN64(1 / b):
+// the hardware approximation (rcp.approx.ftz.f64) refined by two
+// Newton-Raphson steps y += y * (1 - b*y), each with two FMAs -- no call,
+// no slow path (b as a double is never subnormal, nor is 1/b).  Zeros and
+// infinities, where the steps would give NaN, are set to IEEE's answer.
+// Checked against IEEE division on all 2^32 floats (bt_selfcheck).
+__device__ __forceinline__ double recip_d(float b) {
+  const double d = (double)b;
+  double y;
+  asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(y) : "d"(d));
+  double e = __fma_rn(-d, y, 1.0);
+  y = __fma_rn(y, e, y);
+  e = __fma_rn(-d, y, 1.0);
+  y = __fma_rn(y, e, y);
+  if (b == 0.0f) y = copysign((double)INFINITY, d);
+  if (fabsf(b) == INFINITY) y = copysign(0.0, d);
+  return y;
+}
+// Correctly rounded a / b for a divisor shared by many elements: with
+// rb = recip_d(b) computed once, RN32(RN64(a * rb)) == RN32(a / b) for all
+// float a, b.  (A quotient of two floats that is not a float lies at least
+// 2^-49 away (relative) from every float rounding midpoint and is never on
+// one; rb errs by at most 2^-52 and the double product adds 2^-53, so it
+// rounds to the same float.  Infinities, zeros and NaNs follow IEEE
+// division.)
+__device__ __forceinline__ float div_by(float a, double rb) {
+  return __double2float_rn(__dmul_rn((double)a, rb));
+}
+#endif
+
 // ---------------------------------------------------------------------------
 // exp: numpy's float32 SIMD algorithm (rational minimax on a Cody-Waite
 // reduced argument).  x*log2(e) is rounded to an integer quadrant q with the
@@ -80,7 +136,11 @@ BT_HD float scale_pow2(float p, int k) {
 // result = that * 2^q.  Overflow above 88.72283935546875 gives +inf,
 // underflow at or below -103.97208404541015625 gives 0, NaN gives NaN.
 // ---------------------------------------------------------------------------
-BT_HD float np_expf(float x) {
+// IEEE_DIV: the quotient P5/Q2 by IEEE division (the form the self-check
+// compares against); otherwise by div_nr on the device (Q2 lies in [0.9,
+// 1.1] and P5 in [0.7, 1.5] on the reduced range).
+template <bool IEEE_DIV = false>
+BT_HD float np_expf_t(float x) {
   const float kXmax = 88.72283935546875f;
   const float kXmin = -103.97208404541015625f;
   if (is_nan(x)) return qnan();
@@ -90,8 +150,8 @@ BT_HD float np_expf(float x) {
   const float kMagic = 12582912.0f;             // 1.5 * 2^23
   const float kLn2Hi = -6.93145752e-1f;
   const float kLn2Lo = -1.42860677e-6f;
-  float q = BT_ADD(BT_MUL(x, kLog2e), kMagic);
-  q = BT_SUB(q, kMagic);
+  const float t = BT_ADD(BT_MUL(x, kLog2e), kMagic);
+  const float q = BT_SUB(t, kMagic);
   float r = BT_FMA(q, kLn2Hi, x);
   r = BT_FMA(q, kLn2Lo, r);
   float num = BT_FMA(5.082762527590693718096e-04f, r, 6.757896990527504603057e-03f);
@@ -101,8 +161,18 @@ BT_HD float np_expf(float x) {
   num = BT_FMA(num, r, 9.999999999980870924916e-01f);
   float den = BT_FMA(2.159509375685829852307e-02f, r, -2.742335390411667452936e-01f);
   den = BT_FMA(den, r, 1.0f);
-  return scale_pow2(BT_DIV(num, den), (int)q);
+#if defined(__CUDA_ARCH__)
+  const float pq = IEEE_DIV ? BT_DIV(num, den) : div_nr(num, den);
+#else
+  const float pq = BT_DIV(num, den);
+#endif
+  // For |x| < 86 the quadrant k lies in [-124, 124], so pq * 2^k is normal
+  // and exact, and it is pq's bits plus k << 23; bits(t) = 0x4B400000 + k,
+  // whose shift by 23 leaves k << 23 (mod 2^32).
+  if (!IEEE_DIV && fabsf(x) < 86.0f) return bits_f(f_bits(pq) + (f_bits(t) << 23));
+  return scale_pow2(pq, (int)q);
 }
+BT_HD float np_expf(float x) { return np_expf_t<false>(x); }
 
 // ---------------------------------------------------------------------------
 // Double-precision sine / cosine without local memory (the library's own
@@ -330,9 +400,17 @@ BT_HD float np_cosf(float x) { return np_sincosf(x, true); }
 
 // Sigmoid exactly as the reference spells it: 1 / (1 + exp(-x))
 // (ref_runtime.py:470-471), each step rounded in float32.
-BT_HD float np_sigmoidf(float x) {
-  return BT_DIV(1.0f, BT_ADD(1.0f, np_expf(-x)));
+// On the device the reciprocal goes through div_nr while 1 + exp(-x) is
+// below 2^120 (then 1/d stays far from the subnormal range).
+template <bool IEEE_DIV = false>
+BT_HD float np_sigmoidf_t(float x) {
+  const float d = BT_ADD(1.0f, np_expf_t<IEEE_DIV>(-x));
+#if defined(__CUDA_ARCH__)
+  if (!IEEE_DIV && d < 0x1p120f) return div_nr(1.0f, d);
+#endif
+  return BT_DIV(1.0f, d);
 }
+BT_HD float np_sigmoidf(float x) { return np_sigmoidf_t<false>(x); }
 
 // ---------------------------------------------------------------------------
 // numpy's pairwise summation of a contiguous float32 run (the inner loop of

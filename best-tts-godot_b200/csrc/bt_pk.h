@@ -100,18 +100,32 @@ __device__ __forceinline__ float2 pk_np_sincos(float2 z) {
   return v;
 }
 
+// a / b of both lanes by div_nr's steps (the reciprocal approximations are
+// scalar; the refinement and correction are two-lane).
+__device__ __forceinline__ float2 pk_div_nr(float2 a, float2 b) {
+  float2 y = make_float2(rcp_approx(b.x), rcp_approx(b.y));
+  const float2 nb = pk_mul(b, pk(-1.0f));
+  const float2 e = pk_fma(nb, y, pk(1.0f));
+  y = pk_fma(y, e, y);
+  const float2 q = pk_mul(a, y);
+  const float2 r = pk_fma(nb, q, a);
+  return pk_fma(r, y, q);
+}
+
 // Both lanes through the scalar np_expf (NaN and the saturated ranges; the
 // scalar function is short, so it stays inline -- no call, no stack frame).
 __device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_expf(x.x), np_expf(x.y)); }
 
-// exp of both lanes, np_expf step for step.  The quadrant k = (int)q is read
+// exp of both lanes, np_expf step for step, for |x| < 86 in both lanes
+// (others -- and NaN -- take the scalar function).  The quadrant k is read
 // from the bits of t = RN(RN(x * log2e) + 1.5*2^23): t lies in [2^23, 2^24)
-// with ulp 1, so t's bits minus those of 1.5*2^23 are q, negatives included.
+// with ulp 1, so bits(t) = 0x4B400000 + k, and since the low nine bits of
+// 0x4B400000 are zero, bits(t) << 23 = k << 23 (mod 2^32).  On this range
+// k lies in [-124, 124] and P5/Q2 in [0.7, 1.5], so pq * 2^k is normal and
+// exact -- numpy's two scaling multiplies round nothing -- and it is formed
+// by adding k << 23 to the bits of pq.
 __device__ __forceinline__ float2 pk_np_exp(float2 x) {
-  const float kXmax = 88.72283935546875f;
-  const float kXmin = -103.97208404541015625f;
-  // NaN fails every comparison and takes the scalar path, like the ranges
-  if (!(x.x < kXmax && x.x > kXmin && x.y < kXmax && x.y > kXmin)) return pk_exp_edge(x);
+  if (!(fabsf(x.x) < 86.0f && fabsf(x.y) < 86.0f)) return pk_exp_edge(x);
   const float kMagic = 12582912.0f;   // 1.5 * 2^23
   // product then sum: lane by lane (two roundings, see pk_add_lanes)
   const float2 t = pk_add_lanes(pk_mul(x, pk(1.442695040888963407359924681001892137f)), pk(kMagic));
@@ -125,13 +139,9 @@ __device__ __forceinline__ float2 pk_np_exp(float2 x) {
   num = pk_fma(num, r, pk(9.999999999980870924916e-01f));
   float2 den = pk_fma(pk(2.159509375685829852307e-02f), r, pk(-2.742335390411667452936e-01f));
   den = pk_fma(den, r, pk(1.0f));
-  const float2 pq = make_float2(BT_DIV(num.x, den.x), BT_DIV(num.y, den.y));
-  // scale_pow2(pq, k): two exact-power multiplies
-  const int kx = (int)(__float_as_uint(t.x) - 0x4B400000u), ky = (int)(__float_as_uint(t.y) - 0x4B400000u);
-  const int kx1 = kx / 2, ky1 = ky / 2;
-  const float2 s1 = make_float2(pow2i(kx1), pow2i(ky1));
-  const float2 s2 = make_float2(pow2i(kx - kx1), pow2i(ky - ky1));
-  return pk_mul(pk_mul(pq, s1), s2);
+  const float2 pq = pk_div_nr(num, den);
+  return make_float2(__uint_as_float(__float_as_uint(pq.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(pq.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // sin of both lanes (see pk_np_sincos)

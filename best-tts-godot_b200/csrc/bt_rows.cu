@@ -168,17 +168,6 @@ __device__ float pw_sum(const float* s, PwPlan& P, F f, bool aligned) {
   return total;
 }
 
-// Correctly rounded a / b for a divisor shared by many elements: with
-// rb = RN64(1 / b) computed once, RN32(RN64(a * rb)) == RN32(a / b) for all
-// float a, b.  (A quotient of two floats that is not a float lies at least
-// 2^-50 away (relative) from every float rounding midpoint and is never on
-// one; the double-precision product errs by at most 2^-52, so it rounds to
-// the same float.  Infinities, zeros and NaNs follow IEEE division.)
-__device__ __forceinline__ double recip_d(float b) { return __ddiv_rn(1.0, (double)b); }
-__device__ __forceinline__ float div_by(float a, double rb) {
-  return __double2float_rn(__dmul_rn((double)a, rb));
-}
-
 // np.max-style block maximum (NaN propagates).
 __device__ float block_max(const float* s, int n, float* red) {
   float m = -INFINITY;
@@ -798,42 +787,48 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
   const WSlice W = warp_slice(smem, n);
   const float* x = a.x;
   warp_rows(W, n, a.rows, [&](int64_t row) { return x + row * (int64_t)n; }, [&](int64_t row, float* b) {
+    const float* mr = nullptr;
     if (a.mask) {
       // the mask row of this row: lane 0 unravels the row index (64-bit
       // division) only when the mask varies along the leading axes
       long long moff = 0;
       if (!a.mask_row_const) {
         if (lane == 0) {
-          int64_t rem = row;
+          // 32-bit division: the host sends this kernel fewer than 2^32 rows
+          uint32_t rem = (uint32_t)row;
           for (int d = a.lead_rank - 1; d >= 0; --d) {
-            const int64_t c = rem % a.lead_shape[d];
-            rem /= a.lead_shape[d];
-            moff += c * a.mask_lead_st[d];
+            const uint32_t ext = (uint32_t)a.lead_shape[d];
+            const uint32_t c = rem % ext;
+            rem /= ext;
+            moff += (long long)c * a.mask_lead_st[d];
           }
         }
         moff = __shfl_sync(0xffffffffu, moff, 0);
       }
-      const float* mr = a.mask + moff;
-      if (a.mask_col_st) {
-        for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], mr[i]);
-      } else {
-        const float mv = mr[0];
-        for (int i = lane; i < n; i += 32) b[i] = BT_ADD(b[i], mv);
-      }
+      mr = a.mask + moff;
     }
-    // np.max (NaN propagates)
+    // the mask Add (when fused) and the row maximum in one pass.  fmaxf
+    // skips NaN where np.max returns it, but the row's result is all NaN
+    // either way: a NaN element's exp is NaN, so the sum and every quotient
+    // are NaN (and with no NaN both maxima are the same float).
     float m = -INFINITY;
-    bool nan = false;
-    for (int i = lane; i < n; i += 32) {
-      const float v = b[i];
-      if (v != v) nan = true;
-      m = fmaxf(m, v);
+    if (mr && a.mask_col_st) {
+      for (int i = lane; i < n; i += 32) {
+        const float v = BT_ADD(b[i], mr[i]);
+        b[i] = v;
+        m = fmaxf(m, v);
+      }
+    } else if (mr) {
+      const float mv = mr[0];
+      for (int i = lane; i < n; i += 32) {
+        const float v = BT_ADD(b[i], mv);
+        b[i] = v;
+        m = fmaxf(m, v);
+      }
+    } else {
+      for (int i = lane; i < n; i += 32) m = fmaxf(m, b[i]);
     }
-    for (int o = 16; o > 0; o >>= 1) {
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      nan |= __shfl_xor_sync(0xffffffffu, (int)nan, o) != 0;
-    }
-    if (nan) m = qnan();
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     // exp(x - max), elements i and i + 32 two at a time (x - m == x + (-m))
     int i = lane;
     for (; i + 32 < n; i += 64) {
@@ -1082,7 +1077,7 @@ extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, c
       if (a.mask_lead_st[d] != 0) a.mask_row_const = 0;
   }
   WPlan wp;
-  if (n <= kWarpRowMax && wplan_for((int)n, &wp)) {
+  if (n <= kWarpRowMax && rows < (1ll << 32) && wplan_for((int)n, &wp)) {
     size_t smem;
     int grid;
     rc = wrow_setup((int)n, rows, &smem, &grid);

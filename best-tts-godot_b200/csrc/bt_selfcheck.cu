@@ -1,0 +1,66 @@
+// bt_selfcheck.cu -- exhaustive device check of the fast division inside the
+// float32 exp and sigmoid and of the double reciprocal behind division by a
+// per-row constant (bt_selfcheck in bt_ops.h).
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "bt_ops.h"
+#include "bt_internal.h"
+#include "bt_core.h"
+#include "bt_pk.h"
+
+namespace bt {
+namespace {
+
+__device__ __forceinline__ bool same_bits(float a, float b) { return __float_as_uint(a) == __float_as_uint(b); }
+
+__global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first, uint64_t count,
+                                                        unsigned long long* mismatches) {
+  unsigned long long bad = 0;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += stride) {
+    const float x = __uint_as_float((uint32_t)(first + i));
+    switch (kind) {
+      case 0:
+        bad += same_bits(np_expf_t<false>(x), np_expf_t<true>(x)) ? 0 : 1;
+        break;
+      case 1: {
+        const float2 e = pk_np_exp(make_float2(x, -x));
+        bad += same_bits(e.x, np_expf_t<true>(x)) ? 0 : 1;
+        bad += same_bits(e.y, np_expf_t<true>(-x)) ? 0 : 1;
+        break;
+      }
+      case 2:
+        bad += same_bits(np_sigmoidf_t<false>(x), np_sigmoidf_t<true>(x)) ? 0 : 1;
+        break;
+      default: {
+        // within one double ulp of IEEE's 1/x; NaN for NaN
+        const double y = recip_d(x), z = __ddiv_rn(1.0, (double)x);
+        const long long dy = __double_as_longlong(y), dz = __double_as_longlong(z);
+        const bool ok = (y != y && z != z) || dy == dz ||
+                        (((dy ^ dz) >= 0) && (dy - dz == 1 || dz - dy == 1) && fabs(z) != INFINITY && z != 0.0);
+        bad += ok ? 0 : 1;
+        break;
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
+}  // namespace
+}  // namespace bt
+
+using namespace bt;
+
+extern "C" int bt_selfcheck(int kind, uint32_t first, uint64_t count, unsigned long long* mismatches) {
+  if (kind < 0 || kind > 3) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
+  if (!mismatches) return set_error(BT_EINVAL, "bt_selfcheck: null counter");
+  if (count > (1ull << 32) || (uint64_t)first + count > (1ull << 32))
+    return set_error(BT_EINVAL, "bt_selfcheck: range past 2^32 bit patterns");
+  if (count == 0) return BT_OK;
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  selfcheck_kernel<<<di.sm_count * 8, 256, 0, cur_stream()>>>(kind, first, count, mismatches);
+  return check_launch("bt_selfcheck");
+}

@@ -235,6 +235,22 @@ int bt_plan_broadcast(int n_ops, const bt_tensor* ops, const int64_t* out_shape,
  * 2 cos, 3 sigmoid, 4 pairwise row sum (n values -> out[0]). */
 int bt_host_math(int kind, const float* in, float* out, int64_t n);
 
+/* ---- device self-check ----------------------------------------------------
+ * Evaluates the device float32 routine `kind` on every input whose bit
+ * pattern lies in first .. first + count - 1 (count up to 2^32) and adds to
+ * *mismatches (a device counter the caller allocates and zeroes) the number
+ * of inputs whose result differs in any bit from the same routine with its
+ * quotient computed by IEEE division.  kind: 0 exp, 1 exp two lanes at a
+ * time (each input paired with its negation), 2 sigmoid, 3 the double
+ * reciprocal behind division by a per-row constant (softmax, layer and
+ * instance norms), which must lie within one double ulp of IEEE's 1/x and
+ * equal it on zeros, infinities and NaN.  Asynchronous on the set stream.
+ * No counterpart in the reference: over all 2^32 inputs it shows that the
+ * library's fast division gives the IEEE quotient, hence numpy's result,
+ * in every use. */
+int bt_selfcheck(int kind, uint32_t first, uint64_t count,
+                 unsigned long long* mismatches);
+
 #ifdef __cplusplus
 }
 #endif
