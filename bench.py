@@ -200,13 +200,21 @@ def adain_bytes(rows, cols, n_src, n_out, has_res):
 
 
 def measure_op(fn, bytes_, flush, reps, torch):
-    """Median CUDA-event time of fn() over reps, L2 flushed before each."""
+    """Median CUDA-event time of fn() over reps, L2 flushed before each: the
+    flush buffer (larger than L2) is written, then read, so that L2 holds only
+    clean lines of it when fn() starts (dirty flush lines would otherwise be
+    written back during fn and charge it DRAM traffic it never asked for).  A
+    short device-side sleep queued after the flush keeps the GPU busy while
+    the host enqueues fn(), so the interval between the events holds fn's
+    kernels only, not the host's dispatch time."""
     import statistics
     for _ in range(3):
         fn()
     times = []
     for _ in range(reps):
         flush.fill_(1.0)
+        flush.sum()
+        torch.cuda._sleep(400_000)   # ~0.2 ms at 1.965 GHz
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()

@@ -401,12 +401,15 @@ BT_HD float np_cosf(float x) { return np_sincosf(x, true); }
 // Sigmoid exactly as the reference spells it: 1 / (1 + exp(-x))
 // (ref_runtime.py:470-471), each step rounded in float32.
 // On the device the reciprocal goes through div_nr while 1 + exp(-x) is
-// below 2^120 (then 1/d stays far from the subnormal range).
+// below 2^120 (then 1/d stays far from the subnormal range), else through
+// recip_d rounded to float (1/d of a float d is never within 2^-47,
+// relative, of a float rounding midpoint, subnormal ones included, and
+// recip_d errs by at most 2^-52): no division subroutine call.
 template <bool IEEE_DIV = false>
 BT_HD float np_sigmoidf_t(float x) {
   const float d = BT_ADD(1.0f, np_expf_t<IEEE_DIV>(-x));
 #if defined(__CUDA_ARCH__)
-  if (!IEEE_DIV && d < 0x1p120f) return div_nr(1.0f, d);
+  if (!IEEE_DIV) return d < 0x1p120f ? div_nr(1.0f, d) : __double2float_rn(recip_d(d));
 #endif
   return BT_DIV(1.0f, d);
 }

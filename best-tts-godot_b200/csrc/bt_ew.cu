@@ -321,14 +321,22 @@ __device__ __forceinline__ float apply_op(const EwArgs& a, float x, float y, flo
   return apply_f32<TRIG>(OP >= 0 ? OP : a.op, x, y, z, a.alpha, a.n_in);
 }
 
-// Four results of one vector (operands k = 0..2, elements j = 0..3).  Sine
-// and cosine run two elements per instruction (bt_pk.h); every other op goes
-// element by element.
+// Four results of one vector (operands k = 0..2, elements j = 0..3).  Sine,
+// cosine, exp and sigmoid run two elements per instruction (bt_pk.h); every
+// other op goes element by element.
 template <int OP>
 __device__ __forceinline__ float4 apply_vec4(const EwArgs& a, float4 x, float4 y, float4 z) {
   if (OP == BT_OP_SIN || OP == BT_OP_COS) {
     const float2 lo = pk_np_sincos<OP == BT_OP_COS>(make_float2(x.x, x.y));
     const float2 hi = pk_np_sincos<OP == BT_OP_COS>(make_float2(x.z, x.w));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  if (OP == BT_OP_EXP) {
+    const float2 lo = pk_np_exp(make_float2(x.x, x.y)), hi = pk_np_exp(make_float2(x.z, x.w));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  if (OP == BT_OP_SIGMOID) {
+    const float2 lo = pk_np_sigmoid(make_float2(x.x, x.y)), hi = pk_np_sigmoid(make_float2(x.z, x.w));
     return make_float4(lo.x, lo.y, hi.x, hi.y);
   }
   return make_float4(apply_op<OP>(a, x.x, y.x, z.x), apply_op<OP>(a, x.y, y.y, z.y), apply_op<OP>(a, x.z, y.z, z.z),
@@ -493,59 +501,82 @@ __global__ void __launch_bounds__(256) ew_rows_kernel(EwArgs a) {
   }
 }
 
-// The same with the op fixed at compile time (OP >= 0, VEC = 4).
+// Inputs of an op with its own compiled kernel: two for the arithmetic
+// binaries, one for the rest.
+template <int OP>
+__host__ __device__ constexpr int fixed_n_in() {
+  return (OP == BT_OP_ADD || OP == BT_OP_SUB || OP == BT_OP_MUL || OP == BT_OP_DIV || OP == BT_OP_POW) ? 2 : 1;
+}
+// Vectors each thread of ew_rows_op_kernel loads before it computes (one
+// where a call to an out-of-line path would otherwise need a stack frame).
+template <int OP>
+__host__ __device__ constexpr int rows_unroll() {
+  return (OP == BT_OP_DIV || OP == BT_OP_SIGMOID || OP == BT_OP_TANH || OP == BT_OP_GELU || OP == BT_OP_POW) ? 1 : 4;
+}
+
+// The same with the op fixed at compile time (OP >= 0, VEC = 4): each thread
+// issues the loads of U vectors of a row, then computes and stores them.
 template <int VEC, int OP>
 __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
   constexpr bool kTrig = !(VEC == 4 && OP < 0);   // see apply_f32
+  constexpr int NIN = fixed_n_in<OP>();
+  constexpr int U = rows_unroll<OP>();
   const int64_t R = a.shape[0], T = a.shape[1];
   const int64_t nv = T / VEC;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t r = blockIdx.y; r < R; r += gridDim.y) {
-    float rowv[3];
+    float rowv[NIN];
 #pragma unroll
-    for (int k = 0; k < 3; ++k)
-      if (k < a.n_in && a.in[k].st[1] == 0) rowv[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0]);
-    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t t = v * VEC;
-      float x[3][VEC];
+    for (int k = 0; k < NIN; ++k)
+      if (a.in[k].st[1] == 0) rowv[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0]);
+    for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
+      float x[U][NIN][VEC];
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        if (k >= a.n_in) break;
-        const Operand& o = a.in[k];
-        if (o.st[1] == 0) {
+      for (int u = 0; u < U; ++u) {
+        const int64_t t = (v0 + u * stride) * VEC;
+        if (v0 + u * stride >= nv) break;
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) x[k][j] = rowv[k];
-        } else if (VEC == 4 && o.dt == BT_F32) {
-          float4 f = (o.st[0] == 0) ? __ldg((const float4*)((const float*)o.p + t))
-                                    : __ldcs((const float4*)((const float*)o.p + r * o.st[0] + t));
-          x[k][0] = f.x; x[k][1] = f.y; x[k][2] = f.z; x[k][3] = f.w;
-        } else {
+        for (int k = 0; k < NIN; ++k) {
+          const Operand& o = a.in[k];
+          if (o.st[1] == 0) {
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) x[k][j] = ld1<float>(o.p, o.dt, r * o.st[0] + t + j);
+            for (int j = 0; j < VEC; ++j) x[u][k][j] = rowv[k];
+          } else if (VEC == 4 && o.dt == BT_F32) {
+            float4 f = (o.st[0] == 0) ? __ldg((const float4*)((const float*)o.p + t))
+                                      : __ldcs((const float4*)((const float*)o.p + r * o.st[0] + t));
+            x[u][k][0] = f.x; x[u][k][1] = f.y; x[u][k][2] = f.z; x[u][k][3] = f.w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) x[u][k][j] = ld1<float>(o.p, o.dt, r * o.st[0] + t + j);
+          }
         }
       }
-      float res[VEC];
-      if constexpr (VEC == 4 && OP >= 0) {
-        const float4 v4 = apply_vec4<OP>(a, f4(x[0]), a.n_in > 1 ? f4(x[1]) : make_float4(0.f, 0.f, 0.f, 0.f),
-                                         a.n_in > 2 ? f4(x[2]) : make_float4(0.f, 0.f, 0.f, 0.f));
-        res[0] = v4.x; res[1] = v4.y; res[2] = v4.z; res[3] = v4.w;
-      } else {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-          res[j] = apply_op<OP, kTrig>(a, x[0][j], a.n_in > 1 ? x[1][j] : 0.f, a.n_in > 2 ? x[2][j] : 0.f);
-      }
-      const int64_t ob = r * a.ost[0] + t;
-      if (VEC == 4 && a.odt == BT_F32) {
-        __stcs((float4*)((float*)a.out + ob), make_float4(res[0], res[1], res[2], res[3]));
-      } else {
+      for (int u = 0; u < U; ++u) {
+        const int64_t t = (v0 + u * stride) * VEC;
+        if (v0 + u * stride >= nv) break;
+        float res[VEC];
+        if constexpr (VEC == 4 && OP >= 0) {
+          const float4 v4 = apply_vec4<OP>(a, f4(x[u][0]), NIN > 1 ? f4(x[u][NIN - 1]) : make_float4(0.f, 0.f, 0.f, 0.f),
+                                           make_float4(0.f, 0.f, 0.f, 0.f));
+          res[0] = v4.x; res[1] = v4.y; res[2] = v4.z; res[3] = v4.w;
+        } else {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, ob + j, res[j]);
+          for (int j = 0; j < VEC; ++j) res[j] = apply_op<OP, kTrig>(a, x[u][0][j], NIN > 1 ? x[u][NIN - 1][j] : 0.f, 0.f);
+        }
+        const int64_t ob = r * a.ost[0] + t;
+        if (VEC == 4 && a.odt == BT_F32) {
+          __stcs((float4*)((float*)a.out + ob), make_float4(res[0], res[1], res[2], res[3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) st1<float>(a.out, a.odt, ob + j, res[j]);
+        }
       }
     }
     // tail of the row
-    for (int64_t t = nv * VEC + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < T;
-         t += (int64_t)gridDim.x * blockDim.x) {
+    for (int64_t t = nv * VEC + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < T; t += stride) {
       float x[3] = {0.f, 0.f, 0.f};
-      for (int k = 0; k < a.n_in; ++k) x[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0] + t * a.in[k].st[1]);
+      for (int k = 0; k < NIN; ++k) x[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0] + t * a.in[k].st[1]);
       st1<float>(a.out, a.odt, r * a.ost[0] + t, apply_op<OP, kTrig>(a, x[0], x[1], x[2]));
     }
   }
@@ -580,6 +611,9 @@ void launch_flat4(int op, int grid, int threads, cudaStream_t s, const EwArgs& a
 }
 
 void launch_rows4(int op, dim3 grid, int threads, cudaStream_t s, const EwArgs& a) {
+  // the compiled kernels read exactly fixed_n_in<OP>() operands
+  const bool binary = op == BT_OP_ADD || op == BT_OP_SUB || op == BT_OP_MUL || op == BT_OP_DIV || op == BT_OP_POW;
+  if (a.n_in != (binary ? 2 : 1)) op = -1;
   switch (op) {
 #define BT_CASE(OPC) \
   case OPC: ew_rows_op_kernel<4, OPC><<<grid, threads, 0, s>>>(a); return;
@@ -667,7 +701,8 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
     }
     if (ok) {
       const int vec = vec_ok ? 4 : 1;
-      int64_t per_row = (p.shape[1] / vec + threads - 1) / threads;
+      const int unroll = vec_ok ? 4 : 1;   // vectors per thread (ew_rows_op_kernel)
+      int64_t per_row = (p.shape[1] / vec + (int64_t)threads * unroll - 1) / ((int64_t)threads * unroll);
       if (per_row < 1) per_row = 1;
       int gy = (int)(p.shape[0] < 65535 ? p.shape[0] : 65535);
       int gx = (int)(per_row > 64 ? 64 : per_row);

@@ -144,6 +144,16 @@ __device__ __forceinline__ float2 pk_np_exp(float2 x) {
                      __uint_as_float(__float_as_uint(pq.y) + (__float_as_uint(t.y) << 23)));
 }
 
+// 1 / (1 + exp(-x)) of both lanes, np_sigmoidf step for step: the quotient
+// through pk_div_nr while both denominators are below 2^120, else lane by
+// lane as np_sigmoidf does.
+__device__ __forceinline__ float2 pk_np_sigmoid(float2 x) {
+  const float2 d = pk_add(pk(1.0f), pk_np_exp(make_float2(-x.x, -x.y)));
+  if (d.x < 0x1p120f && d.y < 0x1p120f) return pk_div_nr(pk(1.0f), d);
+  return make_float2(d.x < 0x1p120f ? div_nr(1.0f, d.x) : __double2float_rn(recip_d(d.x)),
+                     d.y < 0x1p120f ? div_nr(1.0f, d.y) : __double2float_rn(recip_d(d.y)));
+}
+
 // sin of both lanes (see pk_np_sincos)
 template <bool SQUARE, bool CHECKED = true>
 __device__ __forceinline__ float2 pk_np_sin(float2 z) {

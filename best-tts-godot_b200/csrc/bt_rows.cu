@@ -877,6 +877,173 @@ __global__ void __launch_bounds__(256) wrow_layernorm_kernel(WLayerNormArgs A) {
 }
 
 // ---- warp-row host side ------------------------------------------------------
+// ---- staging-free row sums ---------------------------------------------------
+// ReduceSum / ReduceMean of float32 rows read straight from global memory:
+// one warp per row, one lane pair per pairwise leaf.  Lane h of a pair owns
+// numpy's accumulators r[4h .. 4h+3], so at each 8-element step the pair
+// reads 32 contiguous bytes (one float4 each) -- every DRAM sector of the row
+// is fetched once and no shared-memory copy limits how many warps an SM
+// holds.  The leaf sums go into the warp's heap in shared memory; the tree
+// is combined by the warp alone.  Leaves start at multiples of 8 values, so a
+// row whose first value is 16-byte aligned is read with 128-bit loads; other
+// rows with scalar loads.
+constexpr int kDirLeaves = 384;     // kMaxRow / 128
+constexpr int kDirHeap = 1024;      // heap ids < 2^(D+1), D <= 9
+
+struct DPlan {
+  int32_t n, D, n_leaf, perfect;
+  uint32_t inner[kDirHeap / 64];    // bit h: heap node h (< 2^D) is an inner node
+  uint16_t off[kDirLeaves];
+  uint8_t len[kDirLeaves];
+  uint16_t id[kDirLeaves];
+};
+struct DShared {
+  uint16_t off[kDirLeaves];
+  uint16_t id[kDirLeaves];
+  uint8_t len[kDirLeaves];
+  uint32_t inner[kDirHeap / 64];
+};
+struct DReduceArgs {
+  DPlan P;
+  const float* x;
+  int32_t mean;
+  int64_t rows;
+  float* out;
+};
+
+// Sum of K consecutive leaf sums p[0..K) in pairwise order.
+template <int K>
+__device__ __forceinline__ float dir_lane_leaves(const float* p) {
+  float v[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) v[i] = p[i];
+#pragma unroll
+  for (int w = K; w > 1; w >>= 1) {
+#pragma unroll
+    for (int i = 0; i < w / 2; ++i) v[i] = BT_ADD(v[2 * i], v[2 * i + 1]);
+  }
+  return v[0];
+}
+
+__global__ void __launch_bounds__(256) dir_reduce_kernel(DReduceArgs A) {
+  extern __shared__ __align__(16) float dheap[];
+  __shared__ DShared sh;
+  for (int i = threadIdx.x; i < A.P.n_leaf; i += blockDim.x) {
+    sh.off[i] = A.P.off[i];
+    sh.len[i] = A.P.len[i];
+    sh.id[i] = A.P.id[i];
+  }
+  for (int i = threadIdx.x; i < kDirHeap / 64; i += blockDim.x) sh.inner[i] = A.P.inner[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, h = lane & 1, pair = lane >> 1;
+  const unsigned pmask = 3u << (lane & 30);
+  const int n = A.P.n, D = A.P.D, n_leaf = A.P.n_leaf;
+  const bool perfect = A.P.perfect != 0;
+  float* heap = dheap + (threadIdx.x >> 5) * (2 << D);
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < A.rows; row += (int64_t)gridDim.x * 8) {
+    const float* x = A.x + row * n;
+    const bool vec = ((uintptr_t)x & 15) == 0;
+    for (int L = pair; L < n_leaf; L += 16) {
+      const int off = sh.off[L], len = sh.len[L];
+      const int steps = len >> 3;
+      const float* q = x + off + 4 * h;
+      float res = 0.0f;
+      if (steps > 0) {
+        float r0, r1, r2, r3;
+        if (vec) {
+          float4 v = __ldcs(reinterpret_cast<const float4*>(q));
+          r0 = v.x; r1 = v.y; r2 = v.z; r3 = v.w;
+#pragma unroll 4
+          for (int m = 1; m < steps; ++m) {
+            v = __ldcs(reinterpret_cast<const float4*>(q + 8 * m));
+            r0 = BT_ADD(r0, v.x); r1 = BT_ADD(r1, v.y); r2 = BT_ADD(r2, v.z); r3 = BT_ADD(r3, v.w);
+          }
+        } else {
+          r0 = q[0]; r1 = q[1]; r2 = q[2]; r3 = q[3];
+#pragma unroll 4
+          for (int m = 1; m < steps; ++m) {
+            r0 = BT_ADD(r0, q[8 * m]); r1 = BT_ADD(r1, q[8 * m + 1]);
+            r2 = BT_ADD(r2, q[8 * m + 2]); r3 = BT_ADD(r3, q[8 * m + 3]);
+          }
+        }
+        // lane 0: (r0+r1)+(r2+r3); lane 1: (r4+r5)+(r6+r7); numpy adds the two
+        res = BT_ADD(BT_ADD(r0, r1), BT_ADD(r2, r3));
+        res = BT_ADD(res, __shfl_xor_sync(pmask, res, 1));
+      }
+      // the len % 8 remainder (a leaf shorter than 8: all of it, from +0.0)
+      if (h == 0) {
+        for (int i = steps << 3; i < len; ++i) res = BT_ADD(res, x[off + i]);
+        heap[sh.id[L]] = res;
+      }
+    }
+    __syncwarp();
+    float total;
+    if (perfect && D <= 9) {
+      const float* leaf = heap + (1 << D);
+      switch (D) {
+        case 9: total = dir_lane_leaves<16>(leaf + 16 * lane); break;
+        case 8: total = dir_lane_leaves<8>(leaf + 8 * lane); break;
+        case 7: total = dir_lane_leaves<4>(leaf + 4 * lane); break;
+        case 6: total = dir_lane_leaves<2>(leaf + 2 * lane); break;
+        default: total = lane < (1 << D) ? leaf[lane] : 0.0f; break;
+      }
+      const int levels = D < 5 ? D : 5;
+      for (int m = 0; m < levels; ++m) total = BT_ADD(total, __shfl_xor_sync(0xffffffffu, total, 1 << m));
+      total = __shfl_sync(0xffffffffu, total, 0);
+    } else {
+      for (int k = D - 1; k >= 0; --k) {
+        for (int j = lane; j < (1 << k); j += 32) {
+          const int hh = (1 << k) + j;
+          if ((sh.inner[hh >> 5] >> (hh & 31)) & 1u) heap[hh] = BT_ADD(heap[2 * hh], heap[2 * hh + 1]);
+        }
+        __syncwarp();
+      }
+      total = heap[1];
+    }
+    if (lane == 0) A.out[row] = A.mean ? np_mean_from_sum(BT_ADD(0.0f, total), n) : BT_ADD(0.0f, total);
+    __syncwarp();   // the heap is reused by the next row
+  }
+}
+
+void dplan_node(DPlan& p, int h, int lo, int n, bool& ok) {
+  if (n <= kPwLeaf) {
+    if (p.n_leaf >= kDirLeaves || h >= kDirHeap) { ok = false; return; }
+    p.off[p.n_leaf] = (uint16_t)lo;
+    p.len[p.n_leaf] = (uint8_t)n;
+    p.id[p.n_leaf] = (uint16_t)h;
+    ++p.n_leaf;
+    return;
+  }
+  if (2 * h >= kDirHeap) { ok = false; return; }
+  p.inner[h >> 5] |= 1u << (h & 31);
+  const int n2 = (int)pw_split(n);
+  dplan_node(p, 2 * h, lo, n2, ok);
+  dplan_node(p, 2 * h + 1, lo + n2, n - n2, ok);
+}
+
+// The pairwise plan of a row of n values for dir_reduce_kernel (cached).
+bool dplan_for(int n, DPlan* out) {
+  if (n < 1 || n > kMaxRow) return false;
+  static std::mutex mu;
+  static std::map<int, DPlan> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(n);
+  if (it == cache.end()) {
+    DPlan p;
+    memset(&p, 0, sizeof(p));
+    p.n = n;
+    p.D = pw_depth(n);
+    bool ok = p.D <= 9;
+    if (ok) dplan_node(p, 1, 0, n, ok);
+    p.perfect = (ok && p.n_leaf == (1 << p.D)) ? 1 : 0;
+    if (!ok) p.n = -1;
+    it = cache.emplace(n, p).first;
+  }
+  if (it->second.n < 0) return false;
+  *out = it->second;
+  return true;
+}
+
 void wplan_node(WPlan& p, int h, int lo, int n, bool& ok) {
   if (n <= kPwLeaf) {
     if (p.n_leaf >= kWarpLeaves || h >= kWarpHeap) { ok = false; return; }
@@ -1009,6 +1176,21 @@ extern "C" int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int 
     return set_error(BT_EUNSUPPORTED, "bt_reduce: empty reduction is handled by the caller");
   }
   cudaStream_t s = cur_stream();
+  if (I == 1 && x->dtype == BT_F32 && R > kWarpRowMax) {
+    // rows too long for a warp's shared-memory slice: read them straight
+    // from global memory, one warp per row (shorter rows stage through
+    // shared memory, whose coalesced copies measured faster)
+    DPlan dp;
+    DevInfo di;
+    if ((rc = dev_info(&di))) return rc;
+    if (O >= 2ll * di.sm_count * 8 && R <= kMaxRow && dplan_for((int)R, &dp)) {
+      DReduceArgs a{dp, (const float*)x->data, kind == BT_REDUCE_MEAN, O, (float*)out->data};
+      int64_t g = (O + 7) / 8;
+      if (g > 2147483647) g = 2147483647;
+      dir_reduce_kernel<<<(int)g, 256, (size_t)8 * (2 << dp.D) * sizeof(float), s>>>(a);
+      return check_launch("bt_reduce(direct rows)");
+    }
+  }
   if (I == 1) {
     WPlan wp;
     if (R <= kWarpRowMax && wplan_for((int)R, &wp)) {

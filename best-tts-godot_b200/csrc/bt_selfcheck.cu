@@ -11,7 +11,11 @@
 namespace bt {
 namespace {
 
-__device__ __forceinline__ bool same_bits(float a, float b) { return __float_as_uint(a) == __float_as_uint(b); }
+// Same bits, or both NaN (payloads are not compared: numpy's and the parity
+// tests' convention).
+__device__ __forceinline__ bool same_bits(float a, float b) {
+  return __float_as_uint(a) == __float_as_uint(b) || (a != a && b != b);
+}
 
 __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first, uint64_t count,
                                                         unsigned long long* mismatches) {
@@ -32,6 +36,12 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
       case 2:
         bad += same_bits(np_sigmoidf_t<false>(x), np_sigmoidf_t<true>(x)) ? 0 : 1;
         break;
+      case 4: {
+        const float2 g = pk_np_sigmoid(make_float2(x, -x));
+        bad += same_bits(g.x, np_sigmoidf_t<true>(x)) ? 0 : 1;
+        bad += same_bits(g.y, np_sigmoidf_t<true>(-x)) ? 0 : 1;
+        break;
+      }
       default: {
         // within one double ulp of IEEE's 1/x; NaN for NaN
         const double y = recip_d(x), z = __ddiv_rn(1.0, (double)x);
@@ -53,7 +63,7 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
 using namespace bt;
 
 extern "C" int bt_selfcheck(int kind, uint32_t first, uint64_t count, unsigned long long* mismatches) {
-  if (kind < 0 || kind > 3) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
+  if (kind < 0 || kind > 4) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
   if (!mismatches) return set_error(BT_EINVAL, "bt_selfcheck: null counter");
   if (count > (1ull << 32) || (uint64_t)first + count > (1ull << 32))
     return set_error(BT_EINVAL, "bt_selfcheck: range past 2^32 bit patterns");

@@ -240,11 +240,12 @@ int bt_host_math(int kind, const float* in, float* out, int64_t n);
  * pattern lies in first .. first + count - 1 (count up to 2^32) and adds to
  * *mismatches (a device counter the caller allocates and zeroes) the number
  * of inputs whose result differs in any bit from the same routine with its
- * quotient computed by IEEE division.  kind: 0 exp, 1 exp two lanes at a
+ * quotient computed by IEEE division (two NaNs count as equal).  kind: 0 exp, 1 exp two lanes at a
  * time (each input paired with its negation), 2 sigmoid, 3 the double
  * reciprocal behind division by a per-row constant (softmax, layer and
  * instance norms), which must lie within one double ulp of IEEE's 1/x and
- * equal it on zeros, infinities and NaN.  Asynchronous on the set stream.
+ * equal it on zeros, infinities and NaN, 4 sigmoid two lanes at a time
+ * (each input paired with its negation).  Asynchronous on the set stream.
  * No counterpart in the reference: over all 2^32 inputs it shows that the
  * library's fast division gives the IEEE quotient, hence numpy's result,
  * in every use. */

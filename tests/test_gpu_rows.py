@@ -38,6 +38,21 @@ def test_warp_rows_reduce(gpu_runtime, n):
         assert_same(got[k], want[k], f"{k} n={n}")
 
 
+@pytest.mark.parametrize("n", [3001, 8192, 24001, 49152])
+def test_long_rows_reduce(gpu_runtime, n):
+    """Rows longer than the warp-staged kernels take, read straight from
+    global memory by the warp-per-row sum (odd lengths: unaligned rows)."""
+    rng = np.random.default_rng(300 + n)
+    rows = 2400
+    x = (rng.standard_normal((rows, n)) * 3).astype(np.float32)
+    x[11, n // 3] = np.inf
+    env = {"x": x, "ax": np.array([1], np.int64)}
+    nodes = [("ReduceMean", ["x", "ax"], ["m"], {"keepdims": 1}), ("ReduceSum", ["x", "ax"], ["s"], {"keepdims": 0})]
+    got, want = _run_both(gpu_runtime, nodes, env)
+    for k in ("m", "s"):
+        assert_same(got[k], want[k], f"{k} n={n}")
+
+
 @pytest.mark.parametrize("n", LENGTHS)
 def test_warp_rows_softmax(gpu_runtime, n):
     rng = np.random.default_rng(100 + n)

@@ -23,7 +23,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("kind,name", [(0, "exp"), (1, "exp, two lanes"), (2, "sigmoid"),
-                                       (3, "double reciprocal of a row constant")])
+                                       (3, "double reciprocal of a row constant"), (4, "sigmoid, two lanes")])
 def test_fast_division_equals_ieee_on_every_input(lib, kind, name):
     count = torch.zeros(1, dtype=torch.int64, device="cuda")
     _lib.check(lib.bt_selfcheck(kind, 0, 1 << 32, ctypes.c_void_p(count.data_ptr())), "bt_selfcheck")
