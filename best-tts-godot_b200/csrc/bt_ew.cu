@@ -155,7 +155,7 @@ __device__ __forceinline__ float apply_f32(int op, float a, float b, float c, fl
     case BT_OP_SIN: return TRIG ? np_sinf(a) : a;
     case BT_OP_COS: return TRIG ? np_cosf(a) : a;
     case BT_OP_ATAN: return (float)atan((double)a);
-    case BT_OP_TANH: return (float)tanh((double)a);
+    case BT_OP_TANH: return tanh_f(a);
     case BT_OP_SIGMOID: return np_sigmoidf(a);
     case BT_OP_FLOOR: return floorf(a);
     case BT_OP_ROUND: return rintf(a);
@@ -511,7 +511,7 @@ __host__ __device__ constexpr int fixed_n_in() {
 // where a call to an out-of-line path would otherwise need a stack frame).
 template <int OP>
 __host__ __device__ constexpr int rows_unroll() {
-  return (OP == BT_OP_DIV || OP == BT_OP_SIGMOID || OP == BT_OP_TANH || OP == BT_OP_GELU || OP == BT_OP_POW) ? 1 : 4;
+  return (OP == BT_OP_DIV || OP == BT_OP_SIGMOID || OP == BT_OP_GELU || OP == BT_OP_POW) ? 1 : 4;
 }
 
 // The same with the op fixed at compile time (OP >= 0, VEC = 4): each thread
@@ -599,6 +599,10 @@ int grid_for(int64_t work, int threads) {
 #define BT_EW_FIXED_OPS(X) \
   X(BT_OP_ADD) X(BT_OP_SUB) X(BT_OP_MUL) X(BT_OP_DIV) X(BT_OP_POW) X(BT_OP_SQRT) X(BT_OP_EXP) X(BT_OP_SIN) \
   X(BT_OP_COS) X(BT_OP_TANH) X(BT_OP_SIGMOID) X(BT_OP_LEAKYRELU) X(BT_OP_GELU) X(BT_OP_IDENTITY)
+// the row-broadcast kernels: the same without tanh (see launch_rows4)
+#define BT_EW_ROWS_OPS(X) \
+  X(BT_OP_ADD) X(BT_OP_SUB) X(BT_OP_MUL) X(BT_OP_DIV) X(BT_OP_POW) X(BT_OP_SQRT) X(BT_OP_EXP) X(BT_OP_SIN) \
+  X(BT_OP_COS) X(BT_OP_SIGMOID) X(BT_OP_LEAKYRELU) X(BT_OP_GELU) X(BT_OP_IDENTITY)
 
 void launch_flat4(int op, int grid, int threads, cudaStream_t s, const EwArgs& a) {
   switch (op) {
@@ -611,13 +615,15 @@ void launch_flat4(int op, int grid, int threads, cudaStream_t s, const EwArgs& a
 }
 
 void launch_rows4(int op, dim3 grid, int threads, cudaStream_t s, const EwArgs& a) {
-  // the compiled kernels read exactly fixed_n_in<OP>() operands
+  // the compiled kernels read exactly fixed_n_in<OP>() operands; tanh (a
+  // unary op that reaches this path only for a strided input) keeps the
+  // runtime-op kernel, where its double evaluation needs no stack frame
   const bool binary = op == BT_OP_ADD || op == BT_OP_SUB || op == BT_OP_MUL || op == BT_OP_DIV || op == BT_OP_POW;
   if (a.n_in != (binary ? 2 : 1)) op = -1;
   switch (op) {
 #define BT_CASE(OPC) \
   case OPC: ew_rows_op_kernel<4, OPC><<<grid, threads, 0, s>>>(a); return;
-    BT_EW_FIXED_OPS(BT_CASE)
+    BT_EW_ROWS_OPS(BT_CASE)
 #undef BT_CASE
     default: ew_rows_kernel<4><<<grid, threads, 0, s>>>(a); return;
   }

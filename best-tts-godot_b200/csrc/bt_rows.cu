@@ -96,12 +96,18 @@ __device__ void pw_build(PwPlan& P, int n) {
 // squared deviation from a mean (Sub then Mul, each rounded).
 struct PwIdentity {
   __device__ __forceinline__ float operator()(float v) const { return v; }
+  __device__ __forceinline__ float2 two(float2 acc, float2 v) const { return pk_add(acc, v); }
 };
 struct PwSquaredDev {
   float mu;
   __device__ __forceinline__ float operator()(float v) const {
     const float d = BT_SUB(v, mu);
     return BT_MUL(d, d);
+  }
+  // the product feeds an add: lane by lane (see pk_add_lanes)
+  __device__ __forceinline__ float2 two(float2 acc, float2 v) const {
+    const float2 d = pk_add(v, pk(-mu));
+    return pk_add_lanes(acc, pk_mul(d, d));
   }
 };
 
@@ -640,32 +646,11 @@ __device__ __forceinline__ WView wplan_load(const WPlan& P, WShared& sh) {
 // 16-byte phase), rounded to 16 bytes.
 __host__ __device__ inline int wrow_stride(int n) { return kWarpHeap + (((n + 4) + 3) & ~3); }
 
-// numpy's pairwise sum of f(row[i]) over the whole row (all 32 lanes call;
-// every lane returns the sum, before numpy's "+ 0.0").
-template <class F>
-__device__ __forceinline__ float warp_pw_sum(const WView& P, const float* row, float* heap, F f) {
+// Root of the pairwise tree whose leaf sums the warp's lanes have written
+// into heap (all 32 lanes call; every lane returns the root, and the heap is
+// free again on return).
+__device__ __forceinline__ float warp_heap_total(const WView& P, float* heap) {
   const int lane = threadIdx.x & 31;
-  const int j = lane & 7, g = lane >> 3;
-  const unsigned gmask = 0xffu << (lane & 24);
-  for (int L = g; L < P.n_leaf; L += 4) {
-    const int off = P.off[L], len = P.len[L];
-    const int steps = len >> 3, end = steps << 3;
-    const float* q = row + off + j;
-    float acc = -0.0f;                      // -0.0 + x == x: acc starts as numpy's r[j] = a[j]
-#pragma unroll 4
-    for (int m = 0; m < steps; ++m) acc = BT_ADD(acc, f(q[8 * m]));
-    // numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); addition commutes
-    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 1));
-    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 2));
-    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 4));
-    if (steps == 0) acc = 0.0f;             // a run shorter than 8 is summed from +0.0
-    if (len > end) {
-      if (j == 0)
-        for (int i = end; i < len; ++i) acc = BT_ADD(acc, f(row[off + i]));
-      acc = __shfl_sync(gmask, acc, 0, 8);
-    }
-    if (j == 0) heap[P.id[L]] = acc;
-  }
   __syncwarp();
   float total;
   if (P.perfect) {
@@ -686,6 +671,63 @@ __device__ __forceinline__ float warp_pw_sum(const WView& P, const float* row, f
   }
   __syncwarp();                             // the heap is reused by the next sum
   return total;
+}
+
+// numpy's pairwise sum of f(row[i]) over the whole row (all 32 lanes call;
+// every lane returns the sum, before numpy's "+ 0.0").  A row starting on an
+// 8-byte boundary is summed by groups of four lanes, lane j holding numpy's
+// accumulators r[2j] and r[2j+1] as one float2 (eight leaves at a time, one
+// 64-bit load and one two-lane add per step); otherwise by groups of eight
+// lanes, lane j holding r[j].  f.two(acc, v) adds the transformed pair v to
+// acc; f(v) transforms one value.
+template <class F>
+__device__ __forceinline__ float warp_pw_sum(const WView& P, const float* row, float* heap, F f) {
+  const int lane = threadIdx.x & 31;
+  if (((uintptr_t)row & 7) == 0) {
+    const int j = lane & 3, g = lane >> 2;
+    const unsigned gmask = 0xfu << (lane & 28);
+    for (int L = g; L < P.n_leaf; L += 8) {
+      const int off = P.off[L], len = P.len[L];
+      const int steps = len >> 3, end = steps << 3;
+      const float2* q = reinterpret_cast<const float2*>(row + off + 2 * j);
+      float2 acc = pk(-0.0f);               // -0.0 + x == x: acc starts as numpy's r[j] = a[j]
+#pragma unroll 4
+      for (int m = 0; m < steps; ++m) acc = f.two(acc, q[4 * m]);
+      // numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)); addition commutes
+      float t = BT_ADD(acc.x, acc.y);
+      t = BT_ADD(t, __shfl_xor_sync(gmask, t, 1));
+      t = BT_ADD(t, __shfl_xor_sync(gmask, t, 2));
+      if (steps == 0) t = 0.0f;             // a run shorter than 8 is summed from +0.0
+      if (len > end) {
+        if (j == 0)
+          for (int i = end; i < len; ++i) t = BT_ADD(t, f(row[off + i]));
+        t = __shfl_sync(gmask, t, 0, 4);
+      }
+      if (j == 0) heap[P.id[L]] = t;
+    }
+    return warp_heap_total(P, heap);
+  }
+  const int j = lane & 7, g = lane >> 3;
+  const unsigned gmask = 0xffu << (lane & 24);
+  for (int L = g; L < P.n_leaf; L += 4) {
+    const int off = P.off[L], len = P.len[L];
+    const int steps = len >> 3, end = steps << 3;
+    const float* q = row + off + j;
+    float acc = -0.0f;
+#pragma unroll 4
+    for (int m = 0; m < steps; ++m) acc = BT_ADD(acc, f(q[8 * m]));
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 1));
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 2));
+    acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 4));
+    if (steps == 0) acc = 0.0f;
+    if (len > end) {
+      if (j == 0)
+        for (int i = end; i < len; ++i) acc = BT_ADD(acc, f(row[off + i]));
+      acc = __shfl_sync(gmask, acc, 0, 8);
+    }
+    if (j == 0) heap[P.id[L]] = acc;
+  }
+  return warp_heap_total(P, heap);
 }
 
 struct WReduceArgs {
@@ -811,32 +853,60 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
     // skips NaN where np.max returns it, but the row's result is all NaN
     // either way: a NaN element's exp is NaN, so the sum and every quotient
     // are NaN (and with no NaN both maxima are the same float).
+    // 128-bit over the slice's aligned interior [head, head + 4 nvec)
+    int head = (4 - phase4(b)) & 3;
+    if (head > n) head = n;
+    const int nvec = (n - head) >> 2, tail0 = head + 4 * nvec;
+    const bool mvec = mr && a.mask_col_st && phase4(mr) == phase4(b);
     float m = -INFINITY;
     if (mr && a.mask_col_st) {
       for (int i = lane; i < n; i += 32) {
+        if (mvec && i >= head && i < tail0) continue;
         const float v = BT_ADD(b[i], mr[i]);
         b[i] = v;
         m = fmaxf(m, v);
       }
-    } else if (mr) {
-      const float mv = mr[0];
-      for (int i = lane; i < n; i += 32) {
-        const float v = BT_ADD(b[i], mv);
+      if (mvec) {
+        for (int q = lane; q < nvec; q += 32) {
+          float4 v = *reinterpret_cast<const float4*>(b + head + 4 * q);
+          const float4 w = __ldg(reinterpret_cast<const float4*>(mr + head + 4 * q));
+          v = make_float4(BT_ADD(v.x, w.x), BT_ADD(v.y, w.y), BT_ADD(v.z, w.z), BT_ADD(v.w, w.w));
+          *reinterpret_cast<float4*>(b + head + 4 * q) = v;
+          m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+        }
+      }
+    } else {
+      const float mv = mr ? mr[0] : 0.0f;
+      for (int i = lane; i < head; i += 32) {
+        const float v = mr ? BT_ADD(b[i], mv) : b[i];
         b[i] = v;
         m = fmaxf(m, v);
       }
-    } else {
-      for (int i = lane; i < n; i += 32) m = fmaxf(m, b[i]);
+      for (int q = lane; q < nvec; q += 32) {
+        float4 v = *reinterpret_cast<const float4*>(b + head + 4 * q);
+        if (mr) {
+          v = make_float4(BT_ADD(v.x, mv), BT_ADD(v.y, mv), BT_ADD(v.z, mv), BT_ADD(v.w, mv));
+          *reinterpret_cast<float4*>(b + head + 4 * q) = v;
+        }
+        m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+      }
+      for (int i = tail0 + lane; i < n; i += 32) {
+        const float v = mr ? BT_ADD(b[i], mv) : b[i];
+        b[i] = v;
+        m = fmaxf(m, v);
+      }
     }
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // exp(x - max), elements i and i + 32 two at a time (x - m == x + (-m))
-    int i = lane;
-    for (; i + 32 < n; i += 64) {
-      const float2 e = pk_np_exp(pk_add(pk(b[i], b[i + 32]), pk(-m)));
-      b[i] = e.x;
-      b[i + 32] = e.y;
+    __syncwarp();
+    // exp(x - max) (x - m == x + (-m)), 128-bit over the interior
+    const float2 nm = pk(-m);
+    for (int i = lane; i < head; i += 32) b[i] = np_expf(BT_SUB(b[i], m));
+    for (int q = lane; q < nvec; q += 32) {
+      const float4 v = *reinterpret_cast<const float4*>(b + head + 4 * q);
+      const float2 lo = pk_np_exp(pk_add(pk(v.x, v.y), nm)), hi = pk_np_exp(pk_add(pk(v.z, v.w), nm));
+      *reinterpret_cast<float4*>(b + head + 4 * q) = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
-    if (i < n) b[i] = np_expf(BT_SUB(b[i], m));
+    for (int i = tail0 + lane; i < n; i += 32) b[i] = np_expf(BT_SUB(b[i], m));
     __syncwarp();
     const float denom = BT_ADD(0.0f, warp_pw_sum(P, b, W.heap, PwIdentity()));
     const double rd = recip_d(denom);
@@ -868,10 +938,34 @@ __global__ void __launch_bounds__(256) wrow_layernorm_kernel(WLayerNormArgs A) {
     const float sd = BT_SQRT(BT_ADD(var, a.eps));
     const double rsd = recip_d(sd);
     float* o = a.out + row * (int64_t)n;
-    for (int i = lane; i < n; i += 32) {
-      float y = BT_MUL(div_by(BT_SUB(b[i], mu), rsd), ldf(a.gamma, a.gdt, i));
-      if (a.beta) y = BT_ADD(y, ldf(a.beta, a.bdt, i));
-      o[i] = y;
+    // Sub -> Div -> Mul(gamma) [-> Add(beta)], each rounded
+    auto ln = [&](float v, float g, float be) {
+      const float y = BT_MUL(div_by(BT_SUB(v, mu), rsd), g);
+      return a.beta ? BT_ADD(y, be) : y;
+    };
+    const int ph = phase4(b);
+    const bool vec = phase4(o) == ph && a.gdt == BT_F32 && phase4(a.gamma) == ph &&
+                     (!a.beta || (a.bdt == BT_F32 && phase4(a.beta) == ph));
+    if (vec) {
+      // 128-bit over the aligned interior; gamma / beta fp32 at the row's phase
+      int head = (4 - ph) & 3;
+      if (head > n) head = n;
+      const int nvec = (n - head) >> 2, tail0 = head + 4 * nvec;
+      const float* gm = (const float*)a.gamma;
+      const float* bt = (const float*)a.beta;
+      for (int i = lane; i < head; i += 32) o[i] = ln(b[i], gm[i], bt ? bt[i] : 0.0f);
+      for (int q = lane; q < nvec; q += 32) {
+        const int i = head + 4 * q;
+        const float4 v = *reinterpret_cast<const float4*>(b + i);
+        const float4 g = __ldg(reinterpret_cast<const float4*>(gm + i));
+        const float4 be = bt ? __ldg(reinterpret_cast<const float4*>(bt + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        __stcs(reinterpret_cast<float4*>(o + i),
+               make_float4(ln(v.x, g.x, be.x), ln(v.y, g.y, be.y), ln(v.z, g.z, be.z), ln(v.w, g.w, be.w)));
+      }
+      for (int i = tail0 + lane; i < n; i += 32) o[i] = ln(b[i], gm[i], bt ? bt[i] : 0.0f);
+    } else {
+      for (int i = lane; i < n; i += 32)
+        o[i] = ln(b[i], ldf(a.gamma, a.gdt, i), a.beta ? ldf(a.beta, a.bdt, i) : 0.0f);
     }
   });
 }

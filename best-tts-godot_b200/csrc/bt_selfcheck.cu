@@ -1,6 +1,6 @@
-// bt_selfcheck.cu -- exhaustive device check of the fast division inside the
-// float32 exp and sigmoid and of the double reciprocal behind division by a
-// per-row constant (bt_selfcheck in bt_ops.h).
+// bt_selfcheck.cu -- exhaustive device checks of the library's own float32
+// math: the fast division inside exp and sigmoid, the double reciprocal
+// behind division by a per-row constant, and tanh (bt_selfcheck in bt_ops.h).
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "bt_ops.h"
@@ -36,6 +36,15 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
       case 2:
         bad += same_bits(np_sigmoidf_t<false>(x), np_sigmoidf_t<true>(x)) ? 0 : 1;
         break;
+      case 5: {
+        // within one float ulp of the correctly rounded tanh (the double
+        // library tanh rounded to float); NaN for NaN
+        const float g = tanh_f(x), w = __double2float_rn(tanh((double)x));
+        const int gi = (int)__float_as_uint(g), wi = (int)__float_as_uint(w);
+        const bool ok = (g != g && w != w) || gi == wi || ((gi ^ wi) >= 0 && (gi - wi == 1 || wi - gi == 1));
+        bad += ok ? 0 : 1;
+        break;
+      }
       case 4: {
         const float2 g = pk_np_sigmoid(make_float2(x, -x));
         bad += same_bits(g.x, np_sigmoidf_t<true>(x)) ? 0 : 1;
@@ -63,7 +72,7 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
 using namespace bt;
 
 extern "C" int bt_selfcheck(int kind, uint32_t first, uint64_t count, unsigned long long* mismatches) {
-  if (kind < 0 || kind > 4) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
+  if (kind < 0 || kind > 5) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
   if (!mismatches) return set_error(BT_EINVAL, "bt_selfcheck: null counter");
   if (count > (1ull << 32) || (uint64_t)first + count > (1ull << 32))
     return set_error(BT_EINVAL, "bt_selfcheck: range past 2^32 bit patterns");

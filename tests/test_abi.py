@@ -51,7 +51,7 @@ def test_errors_set_message(lib):
     args.n_src = 1
     assert lib.bt_adain_snake(ctypes.byref(args)) == -1     # src[0] null
     assert b"src[0]" in lib.bt_last_error()
-    assert lib.bt_selfcheck(5, 0, 16, None) == -1 and b"kind" in lib.bt_last_error()
+    assert lib.bt_selfcheck(6, 0, 16, None) == -1 and b"kind" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 0, 16, None) == -1 and b"null" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 1, 1 << 32, ctypes.c_void_p(16)) == -1
 

@@ -76,9 +76,13 @@ def test_warp_rows_layernorm(gpu_runtime, n):
     gamma = rng.uniform(0.5, 1.5, n).astype(np.float16)
     beta = (rng.standard_normal(n) * 0.1).astype(np.float32)
     bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
-    env = {"x": x, "skip": skip, "g": gamma, "b": beta, "bias": bias}
+    env = {"x": x, "skip": skip, "g": gamma, "b": beta, "bias": bias, "g32": gamma.astype(np.float32)}
     nodes = [("LayerNormalization", ["x", "g", "b"], ["y"], {"epsilon": 1e-5, "axis": -1}),
-             ("SkipLayerNormalization", ["x", "skip", "g", "b", "bias"], ["z"], {"epsilon": 1e-12})]
+             ("SkipLayerNormalization", ["x", "skip", "g", "b", "bias"], ["z"], {"epsilon": 1e-12}),
+             ("LayerNormalization", ["x", "g32", "b"], ["y32"], {"epsilon": 1e-5, "axis": -1}),
+             ("LayerNormalization", ["x", "g32"], ["y32n"], {"epsilon": 1e-5, "axis": -1})]
     got, want = _run_both(gpu_runtime, nodes, env)
     assert_same(got["y"], want["y"], f"layernorm n={n}")
     assert_same(got["z"], want["z"], f"skip layernorm n={n}")
+    assert_same(got["y32"], want["y32"], f"layernorm fp32 gamma/beta n={n}")
+    assert_same(got["y32n"], want["y32n"], f"layernorm fp32 gamma, no beta n={n}")
