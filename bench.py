@@ -297,6 +297,13 @@ def per_op(rt, torch, peak):
                                             rt._cast_compute(np.float16, np.float32)), 492000000,
           onode("Cast", c, ["X"], {"to": 1}))
     del Xc
+    # DynamicQuantizeLinear of a stage-1-sized activation [1, 512, 4000]
+    # (algorithmic bytes: x read once, y written once, 5 bytes per value)
+    xq = (np.random.default_rng(0).standard_normal((1, 512, 4000)) * 2).astype(np.float32)
+    Xq = dev(xq)
+    entry("dynquant_8MB", lambda: rt.dynamic_quantize(Xq), xq.size * 5 + 5,
+          onode("DynamicQuantizeLinear", {"x": xq}, ["x"]))
+    del Xq
     # >= 256 MB sweep
     n = 64 * 1024 * 1024
     A = torch.randn((8192, 8192), device="cuda")
@@ -322,6 +329,8 @@ def per_op(rt, torch, peak):
     sweep["adain_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt._reduce_block(A3, [2], 1), n * 4, flush, 5, torch)
     sweep["reducemean_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    ms, gbs = measure_op(lambda: rt.dynamic_quantize(A), 5 * n + 5, flush, 5, torch)
+    sweep["dynquant"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     res["sweep_256MB"] = sweep
     return res
 

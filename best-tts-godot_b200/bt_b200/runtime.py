@@ -89,7 +89,7 @@ class BtRuntime:
                "Sigmoid", "Floor", "Round", "Erf", "LeakyRelu", "Clip", "Equal", "Greater", "Less",
                "GreaterOrEqual", "And", "Where", "Cast", "ReduceMean", "ReduceSum", "Softmax",
                "LayerNormalization", "SkipLayerNormalization", "FastGelu", "DequantizeLinear",
-               "Split", "Reshape", "Unsqueeze", "Squeeze")
+               "DynamicQuantizeLinear", "Split", "Reshape", "Unsqueeze", "Squeeze")
 
     def __init__(self, device=None):
         if not torch.cuda.is_available():
@@ -240,6 +240,14 @@ class BtRuntime:
             ins = [q, scale] + ([zp] if zp is not None else [])
             shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
             out = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
+        elif op == "DynamicQuantizeLinear":                     # ref :106-116, :625-630
+            x = dev(0)
+            if np_dtype(x) not in (np.float32, np.float16):
+                x = self._as_f32(x)
+            for name, v in zip(node_output, self.dynamic_quantize(x)):
+                if name:
+                    env[name] = v
+            return
         elif op == "FastGelu":                                  # ref :610-611
             x, b = dev(0), dev(1)
             x = self._as_f32(x)
@@ -346,6 +354,20 @@ class BtRuntime:
             info = np.iinfo(dt)
             v = info.min if low else info.max
         return torch.tensor(np.array(v, dtype=dt)).to(self.device)
+
+    def dynamic_quantize(self, x):
+        """DynamicQuantizeLinear of a float32 / float16 tensor
+        (bt_dynamic_quantize): (y uint8 of x's shape, scale float32 0-d,
+        zero point uint8 0-d)."""
+        x = self._contig(x)
+        y = self._empty(tuple(x.shape), np.uint8)
+        sc = self._empty((), np.float32)
+        zp = self._empty((), np.uint8)
+        self._stream()
+        check(self.lib.bt_dynamic_quantize(tensor_desc(x), tensor_desc(y), sc.data_ptr(), zp.data_ptr()),
+              "bt_dynamic_quantize")
+        self.launches += 2
+        return y, sc, zp
 
     def _as_f32(self, t):
         dt = np_dtype(t)

@@ -1,0 +1,247 @@
+// bt_quant.cu -- DynamicQuantizeLinear as the reference's numpy op computes
+// it (tools/ref_runtime.py:106-116, dispatched at :625-630):
+//
+//   lo = min(0, float(min x)), hi = max(0, float(max x))     Python floats
+//   scale = (hi - lo) / 255, or 1 when that is 0              double
+//   zp = clip(rint(0 - lo / scale), 0, 255)                   double
+//   y = uint8(clip(rint(x / scale) + zp, 0, 255))             x / scale in float32:
+//       numpy 2 turns the Python-float scale into the array's float32
+//
+// Two kernels over one 12-byte scratch record per (device, stream): the first
+// reduces min, max and "NaN seen" into it with atomics (values mapped to
+// order-preserving integers, all identities 0, so one memset clears it); the
+// second has every CTA derive scale and zero point from the record -- the
+// same double arithmetic in every CTA, so all agree -- and quantizes 16
+// values per thread (four 128-bit loads, one 128-bit store).  CTA 0 writes
+// the scale and zero-point outputs.  A NaN anywhere makes numpy's min and max
+// NaN, which Python's min(0.0, nan) and max(0.0, nan) turn into 0: scale 1,
+// zero point 0; the NaN elements themselves become 0 here (numpy's cast of
+// NaN to uint8 is platform-defined; 0 on x86-64).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <map>
+#include <mutex>
+#include <utility>
+#include "bt_ops.h"
+#include "bt_internal.h"
+#include "bt_core.h"
+
+namespace bt {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Order-preserving map of non-NaN floats to unsigned integers.
+__device__ __forceinline__ uint32_t ord_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_ord(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+// scratch[0] = ~ord(min) (atomicMax), scratch[1] = ord(max), scratch[2] = NaN seen
+template <typename T>
+__device__ __forceinline__ float ldx(const T* x, int64_t i) {
+  if constexpr (sizeof(T) == 2) return __half2float(x[i]);
+  else return x[i];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) dq_range_kernel(const T* x, int64_t n, uint32_t* scratch) {
+  float lo = INFINITY, hi = -INFINITY;
+  bool nan = false;
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t i0 = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if constexpr (sizeof(T) == 4) {
+    // 128-bit loads when x is 16-byte aligned
+    if (((uintptr_t)x & 15) == 0) {
+      const int64_t nv = n >> 2;
+      for (int64_t v = i0; v < nv; v += stride) {
+        const float4 f = __ldcs(reinterpret_cast<const float4*>(x) + v);
+        nan |= (f.x != f.x) | (f.y != f.y) | (f.z != f.z) | (f.w != f.w);
+        lo = fminf(lo, fminf(fminf(f.x, f.y), fminf(f.z, f.w)));
+        hi = fmaxf(hi, fmaxf(fmaxf(f.x, f.y), fmaxf(f.z, f.w)));
+      }
+      // the n % 4 tail: threads of CTA 0
+      i0 = (blockIdx.x == 0 && threadIdx.x < (n & 3)) ? (nv << 2) + threadIdx.x : n;
+    }
+  }
+  for (int64_t i = i0; i < n; i += stride) {
+    const float v = ldx(x, i);
+    nan |= v != v;
+    lo = fminf(lo, v);
+    hi = fmaxf(hi, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  nan = __any_sync(0xffffffffu, nan);
+  __shared__ float slo[kThreads / 32], shi[kThreads / 32];
+  __shared__ int snan;
+  if (threadIdx.x == 0) snan = 0;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    slo[threadIdx.x >> 5] = lo;
+    shi[threadIdx.x >> 5] = hi;
+    if (nan) snan = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kThreads / 32; ++w) {
+      lo = fminf(lo, slo[w]);
+      hi = fmaxf(hi, shi[w]);
+    }
+    // an all-NaN share leaves lo = +inf, hi = -inf: the identities
+    if (lo <= hi) {
+      atomicMax(&scratch[0], ~ord_bits(lo));
+      atomicMax(&scratch[1], ord_bits(hi));
+    }
+    if (snan) atomicOr(&scratch[2], 1u);
+  }
+}
+
+struct DqParams {
+  float scale32;   // float32(scale): the divisor of the element quotients
+  float zp;        // zero point, integral in [0, 255]
+  double rscale;   // recip_d(scale32)
+};
+
+// scale and zero point from the range record (every CTA, identically)
+__device__ __forceinline__ DqParams dq_params(const uint32_t* scratch, int64_t n) {
+  double lo = 0.0, hi = 0.0;
+  if (scratch[2] == 0u && n > 0) {
+    const float m = from_ord(~scratch[0]), M = from_ord(scratch[1]);
+    if (m < 0.0f) lo = (double)m;     // min(0.0, float(m)) keeps 0.0 unless m < 0
+    if (M > 0.0f) hi = (double)M;     // max(0.0, float(M)) keeps 0.0 unless M > 0
+  }
+  double scale = __ddiv_rn(__dsub_rn(hi, lo), 255.0);
+  if (scale == 0.0) scale = 1.0;
+  double z = rint(__dsub_rn(0.0, __ddiv_rn(lo, scale)));
+  z = z != z ? 0.0 : fmin(fmax(z, 0.0), 255.0);
+  DqParams p;
+  p.scale32 = __double2float_rn(scale);
+  p.zp = (float)z;
+  p.rscale = recip_d(p.scale32);
+  return p;
+}
+
+__device__ __forceinline__ uint32_t q8(float x, const DqParams& p) {
+  // rint(x / scale) in float32 (the quotient by recip_d / div_by is the
+  // correctly rounded one), + zp (exact for |q| < 2^24; beyond that either
+  // way saturates), clip, NaN -> 0
+  const float v = BT_ADD(rintf(div_by(x, p.rscale)), p.zp);
+  if (!(v > 0.0f)) return 0u;
+  return v >= 255.0f ? 255u : (uint32_t)v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) dq_quantize_kernel(const T* x, int64_t n, const uint32_t* scratch,
+                                                               uint8_t* y, float* scale_out, uint8_t* zp_out) {
+  __shared__ DqParams sp;
+  if (threadIdx.x == 0) sp = dq_params(scratch, n);
+  __syncthreads();
+  const DqParams p = sp;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *scale_out = p.scale32;
+    *zp_out = (uint8_t)p.zp;
+  }
+  const int64_t stride = (int64_t)gridDim.x * kThreads;
+  int64_t done = 0;
+  if constexpr (sizeof(T) == 4) {
+    if (((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0) {
+      // 16 values per thread: four 128-bit loads, one 128-bit store
+      const int64_t ng = n >> 4;
+      for (int64_t g = (int64_t)blockIdx.x * kThreads + threadIdx.x; g < ng; g += stride) {
+        const float4* src = reinterpret_cast<const float4*>(x) + 4 * g;
+        float4 f[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f[k] = __ldcs(src + k);
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[k] = q8(f[k].x, p) | (q8(f[k].y, p) << 8) | (q8(f[k].z, p) << 16) | (q8(f[k].w, p) << 24);
+        __stcs(reinterpret_cast<uint4*>(y) + g, make_uint4(w[0], w[1], w[2], w[3]));
+      }
+      done = ng << 4;
+    }
+  }
+  for (int64_t i = done + (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride)
+    y[i] = (uint8_t)q8(ldx(x, i), p);
+}
+
+// One 16-byte scratch record per (device, stream), allocated on first use.
+int scratch_for(int device, cudaStream_t s, uint32_t** out) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, uint32_t*> records;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(device, s);
+  auto it = records.find(key);
+  if (it == records.end()) {
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, 16);
+    if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_dynamic_quantize: scratch cudaMalloc: %s", cudaGetErrorString(e));
+    it = records.emplace(key, (uint32_t*)p).first;
+  }
+  *out = it->second;
+  return BT_OK;
+}
+
+}  // namespace
+
+// Shared by bt_dynamic_quantize and its no-allocation variant: the launches
+// over a given scratch record.
+int dynamic_quantize_run(const bt_tensor* x, const bt_tensor* y, float* scale_out, uint8_t* zp_out,
+                         uint32_t* scratch) {
+  const int64_t n = numel(x);
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  cudaStream_t s = cur_stream();
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 12, s);
+  if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_dynamic_quantize: memset: %s", cudaGetErrorString(e));
+  int64_t blocks = (n + kThreads * 16 - 1) / (kThreads * 16);
+  const int64_t cap = (int64_t)di.sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (x->dtype == BT_F32) {
+    dq_range_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, scratch);
+    dq_quantize_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, scratch, (uint8_t*)y->data,
+                                                               scale_out, zp_out);
+  } else {
+    dq_range_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, scratch);
+    dq_quantize_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, scratch,
+                                                                (uint8_t*)y->data, scale_out, zp_out);
+  }
+  return check_launch("bt_dynamic_quantize");
+}
+
+int dynamic_quantize_check(const bt_tensor* x, const bt_tensor* y, const float* scale_out, const uint8_t* zp_out,
+                           const char* what) {
+  int rc = check_tensor(x, "x", false);
+  if (rc) return rc;
+  if ((rc = check_tensor(y, "y", false))) return rc;
+  if (!scale_out || !zp_out) return set_error(BT_EINVAL, "%s: null scale or zero-point output", what);
+  if (x->dtype != BT_F32 && x->dtype != BT_F16) return set_error(BT_EDTYPE, "%s: x must be float32 or float16", what);
+  if (y->dtype != BT_U8) return set_error(BT_EDTYPE, "%s: y must be uint8", what);
+  if (!is_contiguous(x) || !is_contiguous(y) || numel(x) != numel(y))
+    return set_error(BT_EUNSUPPORTED, "%s: contiguous x and y of equal size only", what);
+  if (numel(x) == 0) return set_error(BT_ESHAPE, "%s: empty input (numpy's min of an empty array raises)", what);
+  return BT_OK;
+}
+
+}  // namespace bt
+
+using namespace bt;
+
+extern "C" int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out, uint8_t* zp_out) {
+  int rc = dynamic_quantize_check(x, y, scale_out, zp_out, "bt_dynamic_quantize");
+  if (rc) return rc;
+  DevInfo di;
+  if ((rc = dev_info(&di))) return rc;
+  uint32_t* scratch = nullptr;
+  if ((rc = scratch_for(di.device, cur_stream(), &scratch))) return rc;
+  return dynamic_quantize_run(x, y, scale_out, zp_out, scratch);
+}

@@ -221,6 +221,23 @@ int bt_adain_snake(const bt_adain_args* a);
 int bt_resblock_mean_leaky(const float* const* a, const float* const* b,
                            int64_t n, float divisor, float slope, float* out);
 
+/* ---- DynamicQuantizeLinear ------------------------------------------------
+ * y = uint8(clip(rint(x / scale) + zp, 0, 255)) over the n values of x
+ * (float32 or float16, contiguous; y uint8 of the same size), with
+ *   lo = min(0, min x), hi = max(0, max x), scale = (hi - lo) / 255 in
+ *   double (1 when 0), zp = clip(rint(-lo / scale), 0, 255) in double,
+ * and x / scale formed in float32 (numpy 2 casts the Python-float scale to
+ * the array's dtype).  rint rounds half to even.  *scale_out (float32) and
+ * *zp_out (uint8) are device scalars.  A NaN in x gives scale 1, zero point
+ * 0 and 0 at the NaN elements (numpy's uint8 cast of NaN on x86-64).  An
+ * empty x is an error (numpy's min of an empty array raises).  Uses a
+ * 16-byte scratch record per (device, stream), allocated by the first call
+ * on that pair: make that call before capturing the stream in a graph.
+ * replaces: ref_runtime.py:106-116 and :625-630; the minmax / quantize
+ * dispatch pair of executor.gd:1194-1240 (minmax.glsl, quantize.glsl). */
+int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out,
+                        uint8_t* zp_out);
+
 /* ---- host-only helpers (no GPU) ------------------------------------------ */
 /* Broadcast-and-collapse planner used by bt_elementwise: merges adjacent axes
  * that every operand walks contiguously and drops size-1 axes (the behaviour

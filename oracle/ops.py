@@ -119,6 +119,26 @@ def _dequantize(q, scale, zero_point):
     return v * upcast(scale).astype(np.float32)
 
 
+def _dynamic_quantize(x):
+    # ref_runtime.py:106-116 (dispatched at :625-630).  The float32 range is
+    # widened to Python floats and always includes 0; scale and zero point
+    # are Python-float (double) arithmetic; the element quotient x / scale
+    # divides a float32 array by a Python float, which numpy 2 evaluates in
+    # float32, and adding the float64 zero point promotes to float64 before
+    # the clip and the uint8 cast.  Three outputs: y, scale as float32, zero
+    # point as uint8.
+    x = upcast(x).astype(np.float32)
+    lo = min(0.0, float(x.min()))
+    hi = max(0.0, float(x.max()))
+    scale = (hi - lo) / 255.0
+    if scale == 0:
+        scale = 1.0
+    zp = np.clip(np.rint(0.0 - lo / scale), 0.0, 255.0)
+    q = np.rint(x / scale)                   # float32
+    y = np.clip(q + zp, 0.0, 255.0).astype(np.uint8)
+    return y, np.float32(scale), np.uint8(zp)
+
+
 class OracleRuntime:
     """Op-table interpreter with the reference's ``dispatch`` signature."""
 
@@ -188,6 +208,11 @@ class OracleRuntime:
             out = _fast_gelu(x, y)
         elif op == "DequantizeLinear":                        # ref :631-636
             out = _dequantize(x, y, arg(2))
+        elif op == "DynamicQuantizeLinear":                   # ref :625-630
+            for name, v in zip(node_output, _dynamic_quantize(x)):
+                if name:
+                    env[name] = v
+            return
         # -- view ops that the decoder-stage stream threads between the math
         elif op == "Split":                                   # ref :536-547
             axis = at.get("axis", 0)

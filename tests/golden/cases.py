@@ -266,6 +266,21 @@ def cases():
              ("Mul", ["alpha", "a"], ["t"], {}), ("Sin", ["t"], ["s"], {}), ("Pow", ["s", "two"], ["p"], {}),
              ("Mul", ["inv", "p"], ["q"], {}), ("Add", ["a", "q"], ["z"], {})]
     out.append(Case("adain_snake_chain", nodes, env, outputs=["a", "z"]))
+
+    # -- DynamicQuantizeLinear (ref :106-116): mixed signs, one sign only, all
+    # zeros, fp16 input, a range of exactly 255 (scale 1, so x / scale hits
+    # rint's halfway cases), one value, the float32 extremes
+    dq = [("dq_mixed", _n(rng, (2, 64, 50), 2.0)),
+          ("dq_positive", _u(rng, (3, 40))),
+          ("dq_negative", -_u(rng, (3, 40))),
+          ("dq_zeros", np.zeros((5, 7), F32)),
+          ("dq_f16", _n(rng, (4, 33), 3.0, F16)),
+          ("dq_ties", np.array([0.0, 255.0, 0.5, 1.5, 2.5, 3.5, 254.5, -0.0, 100.49999, 7.5], F32)),
+          ("dq_single", np.array([3.7], F32)),
+          ("dq_extremes", np.array([3.0e38, -3.0e38, 1.0, -1.0, 0.0, 1e-30], F32))]
+    for name, v in dq:
+        out.append(Case(name, [("DynamicQuantizeLinear", ["x"], ["y", "sc", "zp"], {})], {"x": v},
+                        outputs=["y", "sc", "zp"]))
     return out
 
 
