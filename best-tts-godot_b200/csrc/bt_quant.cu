@@ -245,3 +245,59 @@ extern "C" int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float
   if ((rc = scratch_for(di.device, cur_stream(), &scratch))) return rc;
   return dynamic_quantize_run(x, y, scale_out, zp_out, scratch);
 }
+
+// ---- DynamicQuantizeLinear without any device allocation --------------------
+// Some callers of this library cannot allocate device memory while they run:
+// an engine that gives each plugin only the buffers from its own pool,
+// sized once at start-up; a serving process whose memory budget is fixed
+// before the first request; a real-time audio or game loop, where a
+// cudaMalloc can synchronise the device or fail under memory pressure in the
+// middle of a frame.  bt_dynamic_quantize keeps its range record in memory it
+// allocates on first use; this variant keeps it in the file-scope array
+// below instead, which every device that loads the library holds until the
+// process exits.  The array holds 256 bytes; a call uses one 16-byte range
+// record whatever the size of x.  All calls on a device share the record:
+// calls whose work overlaps on the GPU (different streams, or host threads
+// racing) corrupt each other's range.
+namespace bt {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 256;
+constexpr size_t kRangeRecordBytes = 16;
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint32_t)];
+
+// The device address of g_noalloc_scratch on the current device, looked up
+// with cudaGetSymbolAddress by the first call on each device (in host code the
+// array's name stands for a host-side shadow, not for device memory).
+int noalloc_scratch(int device, uint32_t** out) {
+  static std::mutex mu;
+  static std::map<int, uint32_t*> addr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = addr.find(device);
+  if (it == addr.end()) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_error(BT_ECUDA, "bt_dynamic_quantize_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    it = addr.emplace(device, (uint32_t*)p).first;
+  }
+  *out = it->second;
+  return BT_OK;
+}
+
+}  // namespace
+}  // namespace bt
+
+extern "C" int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* y, float* scale_out,
+                                           uint8_t* zp_out) {
+  int rc = dynamic_quantize_check(x, y, scale_out, zp_out, "bt_dynamic_quantize_noalloc");
+  if (rc) return rc;
+  if (kRangeRecordBytes > kNoAllocScratchBytes)
+    return set_error(BT_ETOOBIG, "bt_dynamic_quantize_noalloc: needs %zu bytes of scratch, the static array holds %zu",
+                     kRangeRecordBytes, kNoAllocScratchBytes);
+  DevInfo di;
+  if ((rc = dev_info(&di))) return rc;
+  uint32_t* scratch = nullptr;
+  if ((rc = noalloc_scratch(di.device, &scratch))) return rc;
+  return dynamic_quantize_run(x, y, scale_out, zp_out, scratch);
+}

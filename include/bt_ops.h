@@ -237,6 +237,20 @@ int bt_resblock_mean_leaky(const float* const* a, const float* const* b,
  * dispatch pair of executor.gd:1194-1240 (minmax.glsl, quantize.glsl). */
 int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out,
                         uint8_t* zp_out);
+/* The same results as bt_dynamic_quantize for callers that cannot allocate
+ * device memory at run time (an engine that hands plugins only buffers from
+ * its own pool, a serving process with a fixed memory budget, a real-time
+ * loop where an allocation could stall or fail mid-frame): it allocates
+ * nothing.  Its 16-byte range record lives in a 256-byte static device array
+ * that every device loading the library keeps until exit; a request needing
+ * more scratch than that is rejected (BT_ETOOBIG), and none does today.  The
+ * first call on a device looks up the array's device address: make it before
+ * any stream capture.  All calls on a device share the record, so calls that
+ * overlap on the GPU race.
+ * No counterpart in the reference: the reference's executor always allocates
+ * its min/max scratch (executor.gd:1201-1206). */
+int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* y,
+                                float* scale_out, uint8_t* zp_out);
 
 /* ---- host-only helpers (no GPU) ------------------------------------------ */
 /* Broadcast-and-collapse planner used by bt_elementwise: merges adjacent axes
