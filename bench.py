@@ -304,6 +304,16 @@ def per_op(rt, torch, peak):
     entry("dynquant_8MB", lambda: rt.dynamic_quantize(Xq), xq.size * 5 + 5,
           onode("DynamicQuantizeLinear", {"x": xq}, ["x"]))
     del Xq
+    # the integer convolution epilogue of a stage-0 conv output [1, 256, 4000]
+    # (algorithmic bytes: int32 accumulators read, float32 written)
+    gq = torch.Generator(device="cuda").manual_seed(0)
+    accq = torch.randint(-(1 << 24), 1 << 24, (1, 256, 4000), dtype=torch.int32, device="cuda", generator=gq)
+    biasq = torch.randn(256, device="cuda", generator=gq).half()
+    xsq, wsq = torch.tensor(0.0173, device="cuda"), torch.tensor(0.0021, device="cuda").half()
+    entry("conv_epilogue_8MB", lambda: rt.conv_int_epilogue(accq, biasq, xsq, wsq), accq.numel() * 8 + 256 * 2 + 6)
+    # Transpose of a stage-0 activation [2, 256, 4000] -> [2, 4000, 256]
+    Xt = torch.randn((2, 256, 4000), device="cuda", generator=gq)
+    entry("transpose_8MB", lambda: rt.transpose(Xt, [0, 2, 1]), Xt.numel() * 8)
     # >= 256 MB sweep
     n = 64 * 1024 * 1024
     A = torch.randn((8192, 8192), device="cuda")
@@ -331,6 +341,12 @@ def per_op(rt, torch, peak):
     sweep["reducemean_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt.dynamic_quantize(A), 5 * n + 5, flush, 5, torch)
     sweep["dynquant"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    acc3 = A.view(torch.int32).reshape(64, 128, 8192)
+    bias3 = torch.rand(128, device="cuda").half()
+    ms, gbs = measure_op(lambda: rt.conv_int_epilogue(acc3, bias3, xsq, wsq), 8 * n + 128 * 2 + 6, flush, 5, torch)
+    sweep["conv_epilogue"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    ms, gbs = measure_op(lambda: rt.transpose(A3, [0, 2, 1]), 8 * n, flush, 5, torch)
+    sweep["transpose_last2"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     res["sweep_256MB"] = sweep
     return res
 

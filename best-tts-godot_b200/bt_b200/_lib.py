@@ -97,6 +97,7 @@ SIGNATURES = {
     "bt_selfcheck": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]),
     "bt_dynamic_quantize": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
     "bt_dynamic_quantize_noalloc": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
+    "bt_conv_int_epilogue": (ctypes.c_int, [_P(BtTensor)] * 5),
 }
 
 _lib = None

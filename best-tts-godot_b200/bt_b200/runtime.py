@@ -89,7 +89,8 @@ class BtRuntime:
                "Sigmoid", "Floor", "Round", "Erf", "LeakyRelu", "Clip", "Equal", "Greater", "Less",
                "GreaterOrEqual", "And", "Where", "Cast", "ReduceMean", "ReduceSum", "Softmax",
                "LayerNormalization", "SkipLayerNormalization", "FastGelu", "DequantizeLinear",
-               "DynamicQuantizeLinear", "Split", "Reshape", "Unsqueeze", "Squeeze")
+               "DynamicQuantizeLinear", "Split", "Reshape", "Unsqueeze", "Squeeze", "Transpose", "Concat",
+               "Slice", "Expand")
 
     def __init__(self, device=None):
         if not torch.cuda.is_available():
@@ -113,7 +114,8 @@ class BtRuntime:
         hit = self._consts.get(key)
         if hit is not None and hit[0]() is v:
             return hit[1]
-        t = torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+        # (np.ascontiguousarray makes 0-d arrays 1-d: keep the shape)
+        t = torch.from_numpy(np.ascontiguousarray(a).reshape(a.shape)).to(self.device)
         try:
             self._consts[key] = (weakref.ref(v), t)
         except TypeError:
@@ -138,6 +140,94 @@ class BtRuntime:
         check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
         self.launches += 1
         return out
+
+    # ---- data movement: strided copies through the IDENTITY kernel ----------------
+    @staticmethod
+    def _copy_compute(dt):
+        """A compute dtype in which IDENTITY copies dt exactly (float32 keeps
+        the vector paths for fp32 / fp16 data)."""
+        dt = np.dtype(dt)
+        if dt.kind == "f":
+            return np.float64 if dt == np.float64 else np.float32
+        return np.uint64 if dt == np.uint64 else np.int64
+
+    def _copy_desc(self, src_desc, src_dt, out):
+        """IDENTITY from a source descriptor (any strides, negative ones
+        included) into the tensor view `out`, converting to out's dtype."""
+        if out.numel() == 0:
+            return out
+        descs = (_lib.BtTensor * 1)(src_desc)
+        cdt = self._copy_compute(np.result_type(src_dt, np_dtype(out)))
+        attrs = _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(cdt)], 0.0)
+        self._stream()
+        check(self.lib.bt_elementwise(OP["IDENTITY"], 1, descs, tensor_desc(out), attrs), "bt_elementwise(copy)")
+        self.launches += 1
+        return out
+
+    def _materialize(self, view):
+        """Contiguous copy of a torch view (permuted, expanded, narrowed)."""
+        out = self._empty(tuple(view.shape), np_dtype(view))
+        return self._copy_desc(tensor_desc(view), np_dtype(view), out)
+
+    def transpose(self, x, perm):
+        nd = x.dim()
+        perm = list(range(nd))[::-1] if perm is None else [int(p) % max(nd, 1) for p in perm]
+        return self._materialize(x.permute(perm))
+
+    def concat(self, vals, axis):
+        if any(np_dtype(v) == np.float16 for v in vals):                # ref :531-535
+            vals = [self._widen(v) for v in vals]
+        nd = vals[0].dim()
+        axis = int(axis)
+        if not -nd <= axis < nd:
+            raise np.exceptions.AxisError(axis, nd)
+        axis %= nd
+        for v in vals[1:]:
+            if v.dim() != nd or any(v.shape[d] != vals[0].shape[d] for d in range(nd) if d != axis):
+                raise ValueError("all the input array dimensions except for the concatenation axis must match exactly")
+        dt = np.result_type(*[np_dtype(v) for v in vals])
+        shape = list(vals[0].shape)
+        shape[axis] = sum(int(v.shape[axis]) for v in vals)
+        out = self._empty(shape, dt)
+        off = 0
+        for v in vals:
+            n = int(v.shape[axis])
+            if n:
+                self._copy_desc(tensor_desc(v), np_dtype(v), out.narrow(axis, off, n))
+            off += n
+        return out
+
+    def slice(self, x, starts, ends, axes=None, steps=None):
+        """ref_runtime.py:307-325: clamp each (start, end) as the reference
+        does, then apply Python slice semantics (a clamped end of -1 means the
+        last element), and copy the strided view -- negative steps give
+        negative strides, which the copy kernel reads directly."""
+        starts, ends = _host_ints(starts), _host_ints(ends)
+        axes = list(range(len(starts))) if axes is None else _host_ints(axes)
+        steps = [1] * len(starts) if steps is None else _host_ints(steps)
+        nd = x.dim()
+        shape, strides, offset = list(x.shape), list(x.stride()), 0
+        for s_, e_, a, st in zip(starts, ends, axes, steps):
+            a, s_, e_, st = int(a) % nd, int(s_), int(e_), int(st)
+            dim = int(x.shape[a])
+            lo, hi = (0, dim) if st > 0 else (-1, dim - 1)
+            s_ = min(max(s_ + dim if s_ < 0 else s_, lo), hi)
+            e_ = min(max(e_ + dim if e_ < 0 else e_, lo), hi)
+            start, stop, step = slice(s_, e_, st).indices(dim)
+            shape[a] = len(range(start, stop, step))
+            offset += start * strides[a]
+            strides[a] *= step
+        dt = np_dtype(x)
+        out = self._empty(shape, dt)
+        if out.numel() == 0:
+            return out
+        src = make_tensor(x.data_ptr() + offset * x.element_size(), dt, shape, strides)
+        return self._copy_desc(src, dt, out)
+
+    def expand(self, x, shape):
+        shape = np.broadcast_shapes(tuple(x.shape), tuple(int(v) for v in shape))
+        xv = x.reshape((1,) * (len(shape) - x.dim()) + tuple(x.shape)).expand(shape)
+        return self._materialize(xv)
 
     def _widen(self, t):
         """fp16 tensor -> fp32 copy (kernel), other dtypes unchanged."""
@@ -279,6 +369,14 @@ class BtRuntime:
                 if name:
                     env[name] = p
             return
+        elif op == "Transpose":                                 # ref :517-518
+            out = self.transpose(dev(0), at.get("perm"))
+        elif op == "Concat":                                    # ref :531-535
+            out = self.concat([self.to_device(env[i]) for i in node_input if i], at["axis"])
+        elif op == "Slice":                                     # ref :548-549, :307-325
+            out = self.slice(dev(0), arg(1), arg(2), arg(3), arg(4))
+        elif op == "Expand":                                    # ref :553-555
+            out = self.expand(dev(0), _host_ints(arg(1)))
         elif op == "Reshape":                                   # ref :511-516 (view)
             x = dev(0)
             shape = [int(s) for s in _host_ints(arg(1))]
@@ -368,6 +466,18 @@ class BtRuntime:
               "bt_dynamic_quantize")
         self.launches += 2
         return y, sc, zp
+
+    def conv_int_epilogue(self, acc, bias, x_scale, w_scale):
+        """The integer convolution epilogue in one kernel (bt_conv_int_epilogue):
+        float32(acc + int32(floor(bias / s))) * s with s = x_scale * w_scale,
+        acc int32 [B, C, T], bias [C]; returns float32 [B, C, T]."""
+        acc, bias = self._contig(acc), self._contig(bias)
+        out = self._empty(tuple(acc.shape), np.float32)
+        self._stream()
+        check(self.lib.bt_conv_int_epilogue(tensor_desc(acc), tensor_desc(bias), tensor_desc(x_scale),
+                                            tensor_desc(w_scale), tensor_desc(out)), "bt_conv_int_epilogue")
+        self.launches += 1
+        return out
 
     def _as_f32(self, t):
         dt = np_dtype(t)

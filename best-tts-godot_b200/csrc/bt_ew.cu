@@ -582,6 +582,39 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
   }
 }
 
+// Batched two-dimensional transpose, for IDENTITY copies between equal
+// dtypes whose collapsed form is out[b][m][n] (contiguous) =
+// in[b * sb + m + n * sn]: the input runs along m, the output along n.
+// 32 x 32 tiles pass through shared memory (one padding column against bank
+// conflicts), so both the reads (along m) and the writes (along n) are
+// coalesced; a strided element-by-element copy would fetch a 32-byte sector
+// for every 4-byte read.  W is the element's byte width; bits are copied.
+template <typename W>
+__global__ void __launch_bounds__(256) transpose_kernel(const W* in, W* out, int64_t B, int64_t M, int64_t N,
+                                                        int64_t sb, int64_t sn) {
+  __shared__ W tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
+  const int64_t tm = (M + 31) >> 5, tn = (N + 31) >> 5, tiles = B * tm * tn;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t b = t / (tm * tn), r = t - b * tm * tn;
+    const int64_t m0 = (r / tn) << 5, n0 = (r % tn) << 5;
+    const W* src = in + b * sb;
+#pragma unroll
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t m = m0 + tx, n = n0 + k;
+      if (m < M && n < N) tile[k][tx] = src[m + n * sn];
+    }
+    __syncthreads();
+    W* dst = out + b * M * N;
+#pragma unroll
+    for (int k = ty; k < 32; k += 8) {
+      const int64_t m = m0 + k, n = n0 + tx;
+      if (m < M && n < N) dst[m * N + n] = tile[tx][k];
+    }
+    __syncthreads();
+  }
+}
+
 // ---- launch helpers ---------------------------------------------------------------
 int grid_for(int64_t work, int threads) {
   DevInfo di;
@@ -686,6 +719,24 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
 
   cudaStream_t s = cur_stream();
   const int threads = 256;
+  // a transposing copy between equal dtypes: tiled through shared memory
+  if (op == BT_OP_IDENTITY && n_in == 1 && in[0].dtype == out->dtype && (p.rank == 2 || p.rank == 3)) {
+    const int r = p.rank;
+    const int64_t M = p.shape[r - 2], N = p.shape[r - 1], B = r == 3 ? p.shape[0] : 1;
+    const bool out_dense = p.st[1][r - 1] == 1 && p.st[1][r - 2] == N && (r == 2 || p.st[1][0] == M * N);
+    const int64_t sn = p.st[0][r - 1], sb = r == 3 ? p.st[0][0] : 0;
+    if (out_dense && p.st[0][r - 2] == 1 && sn != 1 && M >= 8 && N >= 8) {
+      const int64_t tiles = B * ((M + 31) / 32) * ((N + 31) / 32);
+      const int g = (int)(tiles < 2147483647 ? tiles : 2147483647);
+      switch (dtype_size(out->dtype)) {
+        case 1: transpose_kernel<uint8_t><<<g, 256, 0, s>>>((const uint8_t*)in[0].data, (uint8_t*)out->data, B, M, N, sb, sn); break;
+        case 2: transpose_kernel<uint16_t><<<g, 256, 0, s>>>((const uint16_t*)in[0].data, (uint16_t*)out->data, B, M, N, sb, sn); break;
+        case 4: transpose_kernel<uint32_t><<<g, 256, 0, s>>>((const uint32_t*)in[0].data, (uint32_t*)out->data, B, M, N, sb, sn); break;
+        default: transpose_kernel<uint64_t><<<g, 256, 0, s>>>((const uint64_t*)in[0].data, (uint64_t*)out->data, B, M, N, sb, sn); break;
+      }
+      return check_launch("bt_elementwise(transpose)");
+    }
+  }
   const bool f32_path = (cdt == BT_F32) && op != BT_OP_WHERE && op != BT_OP_AND;
   if (f32_path && p.rank == 1 && a.ost[0] == 1) {
     bool unit = true, vec_ok = aligned_run(out->data, out->dtype, 4);

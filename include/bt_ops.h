@@ -252,6 +252,24 @@ int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out
 int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* y,
                                 float* scale_out, uint8_t* zp_out);
 
+/* ---- integer convolution epilogue ----------------------------------------
+ * The nodes after each ConvInteger of the quantised generator in one pass:
+ *   s   = x_scale * float32(w_scale)          (DynamicQuantizeLinear's scale
+ *                                              times the weight scale)
+ *   bq  = int32(floor(float32(bias) / s))     per channel
+ *   out = float32(acc + bq[c]) * s            acc int32 [B, C, T] -> float32
+ * each step rounded as numpy rounds the reference's op-by-op chain: int32
+ * addition wraps, int32 -> float32 rounds to nearest even, a floor outside
+ * the int32 range (or NaN) becomes INT32_MIN (numpy's cast on x86-64).
+ * x_scale: one float32; w_scale: one float16 / float32; bias [C] float16 /
+ * float32; all device memory.
+ * replaces: the Cast / Mul / Div / Floor / Cast / Reshape / Add / Cast / Mul
+ * nodes after each ConvInteger (ref_runtime.py:446-455, :572-578 per node;
+ * one executor.gd:678-699 dispatch each). */
+int bt_conv_int_epilogue(const bt_tensor* acc, const bt_tensor* bias,
+                         const bt_tensor* x_scale, const bt_tensor* w_scale,
+                         const bt_tensor* out);
+
 /* ---- host-only helpers (no GPU) ------------------------------------------ */
 /* Broadcast-and-collapse planner used by bt_elementwise: merges adjacent axes
  * that every operand walks contiguously and drops size-1 axes (the behaviour

@@ -139,6 +139,34 @@ def _dynamic_quantize(x):
     return y, np.float32(scale), np.uint8(zp)
 
 
+def _slice(x, starts, ends, axes, steps):
+    # ref_runtime.py:307-325 (dispatched at :548-549): each (start, end) is
+    # made non-negative by adding the extent, then clamped to [0, dim] for a
+    # positive step and to [-1, dim - 1] for a negative one, and handed to a
+    # Python slice.  A clamped end of -1 therefore means "the last element"
+    # to numpy -- so a full reversal comes out empty, as in the reference.
+    starts = np.asarray(starts).reshape(-1)
+    ends = np.asarray(ends).reshape(-1)
+    axes = list(range(len(starts))) if axes is None else np.asarray(axes).reshape(-1)
+    steps = [1] * len(starts) if steps is None else np.asarray(steps).reshape(-1)
+    index = [slice(None)] * x.ndim
+    for s, e, a, st in zip(starts, ends, axes, steps):
+        a, s, e, st = int(a) % x.ndim, int(s), int(e), int(st)
+        dim = x.shape[a]
+        lo, hi = (0, dim) if st > 0 else (-1, dim - 1)
+        s = min(max(s + dim if s < 0 else s, lo), hi)
+        e = min(max(e + dim if e < 0 else e, lo), hi)
+        index[a] = slice(s, e, st)
+    return x[tuple(index)]
+
+
+def _concat(vals, axis):
+    # ref_runtime.py:531-535: any fp16 input widens every input to fp32
+    if any(v.dtype == np.float16 for v in vals):
+        vals = [upcast(v) for v in vals]
+    return np.concatenate(vals, axis=axis)
+
+
 class OracleRuntime:
     """Op-table interpreter with the reference's ``dispatch`` signature."""
 
@@ -226,6 +254,15 @@ class OracleRuntime:
                 if name:
                     env[name] = p
             return
+        elif op == "Transpose":                               # ref :517-518
+            out = np.transpose(x, at.get("perm"))
+        elif op == "Concat":                                  # ref :531-535
+            out = _concat([env[i] for i in node_input if i], at["axis"])
+        elif op == "Slice":                                   # ref :548-549
+            out = _slice(x, arg(1), arg(2), arg(3), arg(4))
+        elif op == "Expand":                                  # ref :553-555
+            shape = np.broadcast_shapes(x.shape, tuple(int(v) for v in np.asarray(y).reshape(-1)))
+            out = np.broadcast_to(x, shape).copy()
         elif op == "Reshape":                                 # ref :511-516
             shape = [int(s) for s in np.asarray(y).reshape(-1)]
             if not at.get("allowzero", 0):

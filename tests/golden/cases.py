@@ -281,6 +281,62 @@ def cases():
     for name, v in dq:
         out.append(Case(name, [("DynamicQuantizeLinear", ["x"], ["y", "sc", "zp"], {})], {"x": v},
                         outputs=["y", "sc", "zp"]))
+
+    # -- the integer convolution epilogue as the packed graph spells it after
+    # each generator ConvInteger: bias scale from the activation and weight
+    # scales, the bias quantised to int32, the int32 Add, the (elided) cast to
+    # fp16 and the rescale
+    def conv_epilogue(acc, bias, xs, ws):
+        nodes = [("Cast", ["xs"], ["xs16"], {"to": 10}), ("Mul", ["xs16", "ws"], ["s"], {}),
+                 ("Div", ["bias", "s"], ["bt"], {}), ("Floor", ["bt"], ["bf"], {}),
+                 ("Cast", ["bf"], ["bq"], {"to": 6}), ("Reshape", ["bq", "shp"], ["bqr"], {}),
+                 ("Add", ["acc", "bqr"], ["sum"], {}), ("Cast", ["sum"], ["sumf"], {"to": 10}),
+                 ("Mul", ["sumf", "s"], ["y"], {})]
+        env = {"acc": acc, "bias": bias, "xs": xs, "ws": ws, "shp": np.array([1, -1, 1], np.int64)}
+        return nodes, env
+    acc = rng.integers(-(1 << 22), 1 << 22, (2, 16, 37)).astype(np.int32)
+    acc[0, 3, :4] = [2147483647, 2147483600, -2147483648, -2147483000]      # int32 wrap-around
+    for name, bias, xs, ws in [
+            ("conv_epi_f16", _n(rng, (16,), 0.2, F16), np.float32(0.0137), np.float16(0.0021)),
+            ("conv_epi_f32", _n(rng, (16,), 0.5), np.float32(0.21), np.float32(3.1e-4)),
+            ("conv_epi_tiny_scale", _n(rng, (16,), 10.0, F16), np.float32(1e-6), np.float16(1e-4))]:
+        nodes, env = conv_epilogue(acc, bias, np.array(xs, F32), np.array(ws))
+        out.append(Case(name, nodes, env, outputs=["s", "bq", "y"]))
+
+    # -- data movement (ref :517-555): transposes, concatenation (with the
+    # fp16 widening and integer promotion), slices with negative indices and
+    # steps (including the reference's empty full reversal), expand
+    t4 = _n(rng, (2, 3, 5, 7))
+    for name, perm in [("tr_last2", [0, 1, 3, 2]), ("tr_rotate", [3, 0, 1, 2]), ("tr_default", None)]:
+        at = {} if perm is None else {"perm": perm}
+        out.append(Case(name, [("Transpose", ["x"], ["y"], at)], {"x": t4}))
+    out.append(Case("tr_int64", [("Transpose", ["x"], ["y"], {"perm": [1, 0]})],
+                    {"x": rng.integers(-9, 9, (6, 11)).astype(np.int64)}))
+    out.append(Case("concat_axis1", [("Concat", ["a", "b", "c"], ["y"], {"axis": 1})],
+                    {"a": _n(rng, (2, 3, 4)), "b": _n(rng, (2, 5, 4)), "c": _n(rng, (2, 1, 4))}))
+    out.append(Case("concat_f16_mix", [("Concat", ["a", "b"], ["y"], {"axis": -1})],
+                    {"a": _n(rng, (3, 4), dt=F16), "b": _n(rng, (3, 2))}))
+    out.append(Case("concat_int_promote", [("Concat", ["a", "b"], ["y"], {"axis": 0})],
+                    {"a": rng.integers(-5, 5, (2, 3)).astype(np.int32),
+                     "b": rng.integers(-5, 5, (1, 3)).astype(np.int64)}))
+    s3 = _n(rng, (4, 9, 10))
+    i64 = lambda *v: np.array(v, np.int64)   # noqa: E731
+    for name, ins in [("slice_basic", (i64(1, 2), i64(3, 8), i64(0, 2), None)),
+                      ("slice_neg", (i64(-3), i64(-1), i64(1), None)),
+                      ("slice_step", (i64(0, 1), i64(9, 10), i64(1, 2), i64(2, 3))),
+                      ("slice_back", (i64(8), i64(1), i64(1), i64(-2))),
+                      ("slice_reverse_all", (i64(-1), i64(-(1 << 62)), i64(2), i64(-1))),
+                      ("slice_clamp", (i64(-100), i64(100), i64(0), None))]:
+        env = {"x": s3, "st": ins[0], "en": ins[1], "ax": ins[2]}
+        names = ["x", "st", "en", "ax"]
+        if ins[3] is not None:
+            env["sp"] = ins[3]
+            names.append("sp")
+        out.append(Case(name, [("Slice", names, ["y"], {})], env))
+    out.append(Case("expand_rank", [("Expand", ["x", "shp"], ["y"], {})],
+                    {"x": _n(rng, (3, 1)), "shp": i64(2, 1, 5)}))
+    out.append(Case("expand_f16", [("Expand", ["x", "shp"], ["y"], {})],
+                    {"x": _n(rng, (1, 4), dt=F16), "shp": i64(3, 4)}))
     return out
 
 
