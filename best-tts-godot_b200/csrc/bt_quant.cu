@@ -58,12 +58,20 @@ __global__ void __launch_bounds__(kThreads) dq_range_kernel(const T* x, int64_t 
     // 128-bit loads when x is 16-byte aligned
     if (((uintptr_t)x & 15) == 0) {
       const int64_t nv = n >> 2;
-      for (int64_t v = i0; v < nv; v += stride) {
-        const float4 f = __ldcs(reinterpret_cast<const float4*>(x) + v);
+      const float4* xv = reinterpret_cast<const float4*>(x);
+      auto take = [&](const float4 f) {
         nan |= (f.x != f.x) | (f.y != f.y) | (f.z != f.z) | (f.w != f.w);
         lo = fminf(lo, fminf(fminf(f.x, f.y), fminf(f.z, f.w)));
         hi = fmaxf(hi, fmaxf(fmaxf(f.x, f.y), fmaxf(f.z, f.w)));
+      };
+      int64_t v = i0;
+      // four vectors in flight per thread
+      for (; v + 3 * stride < nv; v += 4 * stride) {
+        const float4 f0 = __ldcs(xv + v), f1 = __ldcs(xv + v + stride);
+        const float4 f2 = __ldcs(xv + v + 2 * stride), f3 = __ldcs(xv + v + 3 * stride);
+        take(f0); take(f1); take(f2); take(f3);
       }
+      for (; v < nv; v += stride) take(__ldcs(xv + v));
       // the n % 4 tail: threads of CTA 0
       i0 = (blockIdx.x == 0 && threadIdx.x < (n & 3)) ? (nv << 2) + threadIdx.x : n;
     }
