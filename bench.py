@@ -439,22 +439,29 @@ def run_b200(args):
                 "share_of_step_time": round(ad_time / max(sum(kind_time.values()), 1e-12), 4)}
     stream_bytes = stream_algorithmic_bytes(S)
 
-    # end to end through the host-buffer API
+    # end to end through the host-buffer API: every step copies its inputs in
+    # from pinned host memory and its result out; the copies of one step
+    # overlap the neighbouring steps' compute (HostPipeline)
+    pipe = dec.host_pipeline(hin, hout)
     for _ in range(args.warmup):
-        dec.run_host(hin, hout)
+        pipe.step()
+    pipe.finish()
+    torch.cuda.synchronize()
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     h2d = d2h = 0
     for _ in range(args.steps):
-        h2d, d2h = dec.run_host(hin, hout)
+        h2d, d2h = pipe.step()
+    pipe.finish()
     f1.record()
     torch.cuda.synchronize()
     barrier()
     e2e_s = max_over_ranks(f0.elapsed_time(f1) / 1e3)
     e2e = {"value": n * args.batch * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": round(1e3 * e2e_s / args.steps, 3),
-           "api": "FusedDecoder.run_host (pinned host buffers, copies on the compute stream)"}
+           "api": "FusedDecoder.host_pipeline(...).step() (pinned host buffers; each step's copies "
+                  "overlap the neighbouring steps' compute)"}
 
     extra = {}
     if rank == 0 and n == 1 and not args.no_per_op:
@@ -529,14 +536,17 @@ def run_profile_adain(args):
     return 0
 
 
-PROFILE_OPS = ("reducemean_c2", "softmax_c3_b16", "layernorm_768")
+PROFILE_OPS = ("reducemean_c2", "softmax_c3_b16", "layernorm_768", "reducemean_8192", "dynquant_256MB",
+               "conv_epilogue_256MB", "transpose_256MB", "tanh_256MB")
 
 
 def run_profile_op(args):
     """One per-op workload, launched warmup + steps times, for ncu:
     'reducemean_c2' (BASELINE c2 ReduceMean, [64,512,2048]), 'softmax_c3_b16'
     (c3 masked softmax at batch 16) or 'layernorm_768' (LayerNormalization
-    over 768 channels of a 256 MB tensor)."""
+    over 768 channels of a 256 MB tensor); the 256 MB sweep's
+    'reducemean_8192', 'dynquant_256MB', 'conv_epilogue_256MB',
+    'transpose_256MB' ([64,128,8192] -> [64,8192,128]) and 'tanh_256MB'."""
     import torch
     from bt_b200 import configs
     from bt_b200.runtime import BtRuntime
@@ -550,10 +560,24 @@ def run_profile_op(args):
         c = configs.c3(batch=16)
         Xs, M = torch.from_numpy(c["X"]).cuda(), torch.from_numpy(c["mask"]).cuda()
         fn = lambda: rt.softmax(Xs, M, -1)
-    else:
+    elif name == "layernorm_768":
         A = torch.randn((64 * 1024 * 1024 // 768, 768), device="cuda")
         g = torch.rand(768, device="cuda")
         fn = lambda: rt.layernorm(A, None, None, g, None, -1, 1e-5)
+    else:
+        A = torch.randn((64, 128, 8192), device="cuda")
+        if name == "reducemean_8192":
+            fn = lambda: rt._reduce_block(A, [2], 1)
+        elif name == "dynquant_256MB":
+            fn = lambda: rt.dynamic_quantize(A)
+        elif name == "conv_epilogue_256MB":
+            acc, b = A.view(torch.int32), torch.rand(128, device="cuda").half()
+            xs, ws = torch.tensor(0.0173, device="cuda"), torch.tensor(0.0021, device="cuda").half()
+            fn = lambda: rt.conv_int_epilogue(acc, b, xs, ws)
+        elif name == "transpose_256MB":
+            fn = lambda: rt.transpose(A, [0, 2, 1])
+        else:
+            fn = lambda: rt.elementwise("TANH", [A], A.shape, np.float32, np.float32)
     for _ in range(args.warmup + args.steps):
         fn()
     torch.cuda.synchronize()

@@ -385,8 +385,13 @@ class FusedDecoder:
         L = []
         st0 = S.stages[0]
         L.append(("ew", "LEAKYRELU", [self.inputs[st0.x_in]], self.out[st0.leaky_in], LEAKY_STAGE))
+        # plan positions the host pipeline synchronises on: the first reader
+        # of each stage's fc buffer and the last item of each stage (after it
+        # the stage's fc buffer is free; the last one writes S.final)
+        self.stage_first, self.stage_last = [], []
         for st in S.stages:
             fc, gains = self.fc_bufs[st.index], self.gain_bufs[st.index]
+            self.stage_first.append(len(L))
             L.append(("ew", "ADD", [fc[:, :, :st.C], self.t["G/const/one"]], gains, 0.0))
             nb = st.noise
             for k, p in enumerate(nb.pairs):
@@ -410,6 +415,7 @@ class FusedDecoder:
             slope = LEAKY_FINAL if last_stage else LEAKY_STAGE
             a = (ctypes.c_void_p * 3)(*[self._ptr(blk.pairs[-1].c2) for blk in st.res])
             b = (ctypes.c_void_p * 3)(*[self._ptr(blk.pairs[-1].h) for blk in st.res])
+            self.stage_last.append(len(L))
             L.append(("mean", a, b, B * st.C * st.T, float(np.float32(slope)), self._ptr(nxt)))
         # elementwise descriptors are built once, here
         plan = []
@@ -424,15 +430,20 @@ class FusedDecoder:
         self.plan = plan
         assert len(plan) == stream_launches(S)
 
-    def launch(self, record=None):
+    def launch(self, record=None, wait=None, signal=None):
         """Issues the stream on the current CUDA stream; returns the number of
         kernel launches.  With ``record`` (a list), each launch is bracketed by
         CUDA events on that stream and ``(kind, rows, cols, n_src, n_out,
-        has_res, start, end)`` is appended (timing of individual kernels)."""
+        has_res, start, end)`` is appended (timing of individual kernels).
+        ``wait`` maps a plan position to CUDA events the stream waits for
+        before that launch; ``signal`` maps a plan position to an event
+        recorded right after it (both used by HostPipeline)."""
         lib = self.lib
         stream = torch.cuda.current_stream(self.device)
         check(lib.bt_set_stream(stream.cuda_stream), "bt_set_stream")
-        for item in self.plan:
+        for pos, item in enumerate(self.plan):
+            for ev in (wait or {}).get(pos, ()):
+                stream.wait_event(ev)
             kind = item[0]
             if record is not None:
                 ev0 = torch.cuda.Event(enable_timing=True)
@@ -453,6 +464,8 @@ class FusedDecoder:
                     record.append((kind, A.rows, A.cols, A.n_src, A.n_out, bool(A.res), ev0, ev1))
                 else:
                     record.append((kind, 0, 0, 0, 0, False, ev0, ev1))
+            if signal and pos in signal:
+                signal[pos].record(stream)
         return len(self.plan)
 
     # ---- end-to-end path (host buffers) ------------------------------------------
@@ -476,6 +489,10 @@ class FusedDecoder:
         for i, st in enumerate(S.stages):
             stacked = np.stack([host[a.fc].reshape(S.batch, 2 * st.C) for a in S.adains(st)])
             hin[f"fc{i}"].copy_(torch.from_numpy(stacked))
+
+    def host_pipeline(self, hin, hout):
+        """A HostPipeline over this decoder and the given host buffers."""
+        return HostPipeline(self, hin, hout)
 
     def run_host(self, hin, hout):
         """One end-to-end step on the current stream: host-to-device copies
@@ -541,3 +558,73 @@ def load_host_inputs(dec, host):
         if name in dec.inputs:
             dec.inputs[name].copy_(torch.from_numpy(np.ascontiguousarray(arr)).reshape(dec.inputs[name].shape),
                                    non_blocking=False)
+
+
+class HostPipeline:
+    """End-to-end steps whose host transfers overlap the neighbouring steps'
+    compute (the serving loop of the host-buffer API).
+
+    Each ``step()`` copies the step's inputs from the pinned host buffers,
+    runs the fused stream on the current stream and copies the final stage
+    output back, like ``FusedDecoder.run_host``, but with the copies on two
+    side streams (host-to-device and device-to-host run concurrently over the
+    full-duplex link), ordered by events instead of by the compute stream:
+
+    - the features of step i+1 are copied once step i's first kernel has
+      read them, each stage's fc outputs once step i's last kernel of that
+      stage has run;
+    - step i's result is copied out while step i+1 computes; step i+1's last
+      kernel, which rewrites that buffer, waits for the copy.
+
+    ``finish()`` makes the current stream wait for the last copy-out; after
+    it, ``hout`` holds the last step's result."""
+
+    def __init__(self, dec, hin, hout):
+        self.dec, self.hin, self.hout = dec, hin, hout
+        self.h2d = torch.cuda.Stream(dec.device)
+        self.d2h = torch.cuda.Stream(dec.device)
+        self.prev = None
+
+    def step(self):
+        dec, S = self.dec, self.dec.S
+        comp = torch.cuda.current_stream(dec.device)
+        feat = S.stages[0].x_in
+        prev = self.prev
+        ev = lambda: torch.cuda.Event()   # noqa: E731
+        cur = {"feat_free": ev(), "fc_free": [ev() for _ in S.stages], "d2h_done": ev()}
+        feat_ready, fc_ready = ev(), [ev() for _ in S.stages]
+        h2d = self.hin[feat].numel() * 4
+        with torch.cuda.stream(self.h2d):
+            if prev is None:
+                self.h2d.wait_stream(comp)
+            else:
+                self.h2d.wait_event(prev["feat_free"])
+            dec.inputs[feat].copy_(self.hin[feat], non_blocking=True)
+            feat_ready.record(self.h2d)
+            for i, fc in enumerate(dec.fc_bufs):
+                if prev is not None:
+                    self.h2d.wait_event(prev["fc_free"][i])
+                fc.copy_(self.hin[f"fc{i}"], non_blocking=True)
+                fc_ready[i].record(self.h2d)
+                h2d += fc.numel() * 4
+        wait = {0: [feat_ready]}
+        for i, pos in enumerate(dec.stage_first):
+            wait.setdefault(pos, []).append(fc_ready[i])
+        last = dec.stage_last[-1]
+        if prev is not None:
+            wait.setdefault(last, []).append(prev["d2h_done"])
+        signal = {0: cur["feat_free"]}
+        for i, pos in enumerate(dec.stage_last):
+            signal[pos] = cur["fc_free"][i]
+        out_ready = cur["fc_free"][-1]   # the last stage's last kernel writes S.final
+        dec.launch(wait=wait, signal=signal)
+        with torch.cuda.stream(self.d2h):
+            self.d2h.wait_event(out_ready)
+            self.hout.copy_(dec.out[S.final], non_blocking=True)
+            cur["d2h_done"].record(self.d2h)
+        self.prev = cur
+        return h2d, self.hout.numel() * 4
+
+    def finish(self):
+        if self.prev is not None:
+            torch.cuda.current_stream(self.dec.device).wait_event(self.prev["d2h_done"])

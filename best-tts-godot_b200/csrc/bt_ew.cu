@@ -392,9 +392,11 @@ __global__ void __launch_bounds__(256) ew_flat_kernel(EwArgs a) {
   }
 }
 
-// The same with the op fixed at compile time (OP >= 0, VEC = 4).
+// The same with the op fixed at compile time (OP >= 0, VEC = 4).  (Tanh
+// declares a minimum of one CTA per SM: ptxas then keeps its double
+// evaluation in registers; without a minimum it chose fewer and spilled.)
 template <int VEC, int OP>
-__global__ void __launch_bounds__(256) ew_flat_op_kernel(EwArgs a) {
+__global__ void __launch_bounds__(256, OP == BT_OP_TANH ? 1 : 0) ew_flat_op_kernel(EwArgs a) {
   constexpr bool kTrig = !(VEC == 4 && OP < 0);   // see apply_f32
   const int64_t nv = a.n / VEC;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -594,22 +596,33 @@ __global__ void __launch_bounds__(256) transpose_kernel(const W* in, W* out, int
                                                         int64_t sb, int64_t sn) {
   __shared__ W tile[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
-  const int64_t tm = (M + 31) >> 5, tn = (N + 31) >> 5, tiles = B * tm * tn;
+  // tile coordinates in 32-bit (the host sends M, N < 2^30)
+  const int tm = (int)((M + 31) >> 5), tn = (int)((N + 31) >> 5);
+  const int64_t per_b = (int64_t)tm * tn, tiles = B * per_b;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int64_t b = t / (tm * tn), r = t - b * tm * tn;
-    const int64_t m0 = (r / tn) << 5, n0 = (r % tn) << 5;
-    const W* src = in + b * sb;
+    const int64_t b = t / per_b;
+    const int r = (int)(t - b * per_b);
+    const int m0 = (r / tn) << 5, n0 = (r % tn) << 5;
+    const W* src = in + b * sb + m0 + (int64_t)n0 * sn;   // element (m0, n0) of batch b
+    W* dst = out + b * M * N + (int64_t)m0 * N + n0;       // element (m0, n0) of the output
+    if (m0 + 32 <= M && n0 + 32 <= N) {
+      // a full tile: no bounds checks
+      const W* s0 = src + tx + ty * sn;
 #pragma unroll
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t m = m0 + tx, n = n0 + k;
-      if (m < M && n < N) tile[k][tx] = src[m + n * sn];
-    }
-    __syncthreads();
-    W* dst = out + b * M * N;
+      for (int k = 0; k < 32; k += 8) tile[ty + k][tx] = s0[k * sn];
+      __syncthreads();
+      W* d0 = dst + tx + (int64_t)ty * N;
 #pragma unroll
-    for (int k = ty; k < 32; k += 8) {
-      const int64_t m = m0 + k, n = n0 + tx;
-      if (m < M && n < N) dst[m * N + n] = tile[tx][k];
+      for (int k = 0; k < 32; k += 8) d0[(int64_t)k * N] = tile[tx][ty + k];
+    } else {
+      const int mr = (int)(M - m0 < 32 ? M - m0 : 32), nr = (int)(N - n0 < 32 ? N - n0 : 32);
+#pragma unroll
+      for (int k = ty; k < 32; k += 8)
+        if (tx < mr && k < nr) tile[k][tx] = src[tx + k * sn];
+      __syncthreads();
+#pragma unroll
+      for (int k = ty; k < 32; k += 8)
+        if (k < mr && tx < nr) dst[(int64_t)k * N + tx] = tile[tx][k];
     }
     __syncthreads();
   }
@@ -725,7 +738,7 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
     const int64_t M = p.shape[r - 2], N = p.shape[r - 1], B = r == 3 ? p.shape[0] : 1;
     const bool out_dense = p.st[1][r - 1] == 1 && p.st[1][r - 2] == N && (r == 2 || p.st[1][0] == M * N);
     const int64_t sn = p.st[0][r - 1], sb = r == 3 ? p.st[0][0] : 0;
-    if (out_dense && p.st[0][r - 2] == 1 && sn != 1 && M >= 8 && N >= 8) {
+    if (out_dense && p.st[0][r - 2] == 1 && sn != 1 && M >= 8 && N >= 8 && M < (1ll << 30) && N < (1ll << 30)) {
       const int64_t tiles = B * ((M + 31) / 32) * ((N + 31) / 32);
       const int g = (int)(tiles < 2147483647 ? tiles : 2147483647);
       switch (dtype_size(out->dtype)) {

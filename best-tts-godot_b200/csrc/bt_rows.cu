@@ -971,16 +971,7 @@ __global__ void __launch_bounds__(256) wrow_layernorm_kernel(WLayerNormArgs A) {
 }
 
 // ---- warp-row host side ------------------------------------------------------
-// ---- staging-free row sums ---------------------------------------------------
-// ReduceSum / ReduceMean of float32 rows read straight from global memory:
-// one warp per row, one lane pair per pairwise leaf.  Lane h of a pair owns
-// numpy's accumulators r[4h .. 4h+3], so at each 8-element step the pair
-// reads 32 contiguous bytes (one float4 each) -- every DRAM sector of the row
-// is fetched once and no shared-memory copy limits how many warps an SM
-// holds.  The leaf sums go into the warp's heap in shared memory; the tree
-// is combined by the warp alone.  Leaves start at multiples of 8 values, so a
-// row whose first value is 16-byte aligned is read with 128-bit loads; other
-// rows with scalar loads.
+// ---- pairwise plans for rows up to kMaxRow values -------------------------
 constexpr int kDirLeaves = 384;     // kMaxRow / 128
 constexpr int kDirHeap = 1024;      // heap ids < 2^(D+1), D <= 9
 
@@ -997,14 +988,6 @@ struct DShared {
   uint8_t len[kDirLeaves];
   uint32_t inner[kDirHeap / 64];
 };
-struct DReduceArgs {
-  DPlan P;
-  const float* x;
-  int32_t mean;
-  int64_t rows;
-  float* out;
-};
-
 // Sum of K consecutive leaf sums p[0..K) in pairwise order.
 template <int K>
 __device__ __forceinline__ float dir_lane_leaves(const float* p) {
@@ -1019,84 +1002,166 @@ __device__ __forceinline__ float dir_lane_leaves(const float* p) {
   return v[0];
 }
 
-__global__ void __launch_bounds__(256) dir_reduce_kernel(DReduceArgs A) {
-  extern __shared__ __align__(16) float dheap[];
+// ---- chunked row sums -----------------------------------------------------
+// ReduceSum / ReduceMean of float32 rows longer than a warp's shared-memory
+// slice, one warp per row, the row streamed through two buffers of kChunk
+// values: while the warp sums the pairwise leaves of one run of whole leaves
+// (a chunk), the cp.async copy of the next run -- of this row or of the
+// warp's next row -- is in flight.  Copies are coalesced 16-byte transfers;
+// the leaves are summed as in warp_pw_sum (four lanes per leaf with float2
+// accumulators on 8-byte aligned rows, eight otherwise).
+constexpr int kChunk = 1024;
+
+struct CReduceArgs {
+  DPlan P;
+  uint16_t chunk_leaf[kDirLeaves + 1];   // chunk c holds leaves [chunk_leaf[c], chunk_leaf[c + 1])
+  int32_t n_chunk;
+  const float* x;
+  int32_t mean;
+  int64_t rows;
+  float* out;
+};
+
+// Per-warp shared floats of chunk_reduce_kernel: the heap, then two buffers
+// (kChunk values + 4 for the 16-byte phase each).
+__host__ __device__ inline int chunk_warp_floats(int D) { return (2 << D) + 2 * (kChunk + 4); }
+
+__global__ void __launch_bounds__(256) chunk_reduce_kernel(CReduceArgs A) {
+  extern __shared__ __align__(16) float csm[];
   __shared__ DShared sh;
+  __shared__ uint16_t schunk[kDirLeaves + 1];
   for (int i = threadIdx.x; i < A.P.n_leaf; i += blockDim.x) {
     sh.off[i] = A.P.off[i];
     sh.len[i] = A.P.len[i];
     sh.id[i] = A.P.id[i];
   }
+  for (int i = threadIdx.x; i <= A.n_chunk; i += blockDim.x) schunk[i] = A.chunk_leaf[i];
   for (int i = threadIdx.x; i < kDirHeap / 64; i += blockDim.x) sh.inner[i] = A.P.inner[i];
   __syncthreads();
-  const int lane = threadIdx.x & 31, h = lane & 1, pair = lane >> 1;
-  const unsigned pmask = 3u << (lane & 30);
-  const int n = A.P.n, D = A.P.D, n_leaf = A.P.n_leaf;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = A.P.n, D = A.P.D, n_leaf = A.P.n_leaf, nch = A.n_chunk;
   const bool perfect = A.P.perfect != 0;
-  float* heap = dheap + (threadIdx.x >> 5) * (2 << D);
-  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < A.rows; row += (int64_t)gridDim.x * 8) {
-    const float* x = A.x + row * n;
-    const bool vec = ((uintptr_t)x & 15) == 0;
-    for (int L = pair; L < n_leaf; L += 16) {
-      const int off = sh.off[L], len = sh.len[L];
-      const int steps = len >> 3;
-      const float* q = x + off + 4 * h;
-      float res = 0.0f;
-      if (steps > 0) {
-        float r0, r1, r2, r3;
-        if (vec) {
-          float4 v = __ldcs(reinterpret_cast<const float4*>(q));
-          r0 = v.x; r1 = v.y; r2 = v.z; r3 = v.w;
-#pragma unroll 4
-          for (int m = 1; m < steps; ++m) {
-            v = __ldcs(reinterpret_cast<const float4*>(q + 8 * m));
-            r0 = BT_ADD(r0, v.x); r1 = BT_ADD(r1, v.y); r2 = BT_ADD(r2, v.z); r3 = BT_ADD(r3, v.w);
-          }
-        } else {
-          r0 = q[0]; r1 = q[1]; r2 = q[2]; r3 = q[3];
-#pragma unroll 4
-          for (int m = 1; m < steps; ++m) {
-            r0 = BT_ADD(r0, q[8 * m]); r1 = BT_ADD(r1, q[8 * m + 1]);
-            r2 = BT_ADD(r2, q[8 * m + 2]); r3 = BT_ADD(r3, q[8 * m + 3]);
-          }
-        }
-        // lane 0: (r0+r1)+(r2+r3); lane 1: (r4+r5)+(r6+r7); numpy adds the two
-        res = BT_ADD(BT_ADD(r0, r1), BT_ADD(r2, r3));
-        res = BT_ADD(res, __shfl_xor_sync(pmask, res, 1));
-      }
-      // the len % 8 remainder (a leaf shorter than 8: all of it, from +0.0)
-      if (h == 0) {
-        for (int i = steps << 3; i < len; ++i) res = BT_ADD(res, x[off + i]);
-        heap[sh.id[L]] = res;
-      }
+  float* heap = csm + warp * chunk_warp_floats(D);
+  float* const buf0 = heap + (2 << D);   // buffer `slot` starts at buf0 + slot * (kChunk + 4)
+  const int64_t rstride = (int64_t)gridDim.x * 8;
+  int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= A.rows) return;
+  auto chunk_lo = [&](int c) { return (int)sh.off[schunk[c]]; };
+  auto chunk_hi = [&](int c) { return schunk[c + 1] < n_leaf ? (int)sh.off[schunk[c + 1]] : n; };
+  auto issue = [&](int64_t row, int c, int slot) {
+    const float* g = A.x + row * n + chunk_lo(c);
+    stage_floats_async(buf0 + slot * (kChunk + 4) + phase4(g), g, chunk_hi(c) - chunk_lo(c), lane, 32);
+    cp_async_commit();
+  };
+  issue(r, 0, 0);
+  int c = 0, slot = 0;
+  while (r < A.rows) {
+    int64_t rn = r;
+    int cn = c + 1;
+    if (cn == nch) {
+      cn = 0;
+      rn += rstride;
     }
+    if (rn < A.rows) issue(rn, cn, slot ^ 1);
+    else cp_async_commit();          // an empty group keeps the count
+    cp_async_wait<1>();              // this chunk's copies (this lane's)
     __syncwarp();
-    float total;
-    if (perfect && D <= 9) {
-      const float* leaf = heap + (1 << D);
-      switch (D) {
-        case 9: total = dir_lane_leaves<16>(leaf + 16 * lane); break;
-        case 8: total = dir_lane_leaves<8>(leaf + 8 * lane); break;
-        case 7: total = dir_lane_leaves<4>(leaf + 4 * lane); break;
-        case 6: total = dir_lane_leaves<2>(leaf + 2 * lane); break;
-        default: total = lane < (1 << D) ? leaf[lane] : 0.0f; break;
-      }
-      const int levels = D < 5 ? D : 5;
-      for (int m = 0; m < levels; ++m) total = BT_ADD(total, __shfl_xor_sync(0xffffffffu, total, 1 << m));
-      total = __shfl_sync(0xffffffffu, total, 0);
-    } else {
-      for (int k = D - 1; k >= 0; --k) {
-        for (int j = lane; j < (1 << k); j += 32) {
-          const int hh = (1 << k) + j;
-          if ((sh.inner[hh >> 5] >> (hh & 31)) & 1u) heap[hh] = BT_ADD(heap[2 * hh], heap[2 * hh + 1]);
+    const int e0 = chunk_lo(c);
+    const float* g = A.x + r * n + e0;
+    const float* b = buf0 + slot * (kChunk + 4) + phase4(g);   // b[e - e0]: value e of the row
+    const int l0 = schunk[c], l1 = schunk[c + 1];
+    if (((uintptr_t)b & 7) == 0) {
+      const int j = lane & 3;
+      const unsigned gmask = 0xfu << (lane & 28);
+      for (int L = l0 + (lane >> 2); L < l1; L += 8) {
+        const int off = sh.off[L] - e0, len = sh.len[L];
+        const int steps = len >> 3, end = steps << 3;
+        const float2* q = reinterpret_cast<const float2*>(b + off + 2 * j);
+        float2 acc = pk(-0.0f);      // -0.0 + x == x: acc starts as numpy's r[j] = a[j]
+#pragma unroll 4
+        for (int m = 0; m < steps; ++m) acc = pk_add(acc, q[4 * m]);
+        float t = BT_ADD(acc.x, acc.y);
+        t = BT_ADD(t, __shfl_xor_sync(gmask, t, 1));
+        t = BT_ADD(t, __shfl_xor_sync(gmask, t, 2));
+        if (steps == 0) t = 0.0f;
+        if (len > end) {
+          if (j == 0)
+            for (int i = end; i < len; ++i) t = BT_ADD(t, b[off + i]);
+          t = __shfl_sync(gmask, t, 0, 4);
         }
-        __syncwarp();
+        if (j == 0) heap[sh.id[L]] = t;
       }
-      total = heap[1];
+    } else {
+      const int j = lane & 7;
+      const unsigned gmask = 0xffu << (lane & 24);
+      for (int L = l0 + (lane >> 3); L < l1; L += 4) {
+        const int off = sh.off[L] - e0, len = sh.len[L];
+        const int steps = len >> 3, end = steps << 3;
+        const float* q = b + off + j;
+        float acc = -0.0f;
+#pragma unroll 4
+        for (int m = 0; m < steps; ++m) acc = BT_ADD(acc, q[8 * m]);
+        acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 1));
+        acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 2));
+        acc = BT_ADD(acc, __shfl_xor_sync(gmask, acc, 4));
+        if (steps == 0) acc = 0.0f;
+        if (len > end) {
+          if (j == 0)
+            for (int i = end; i < len; ++i) acc = BT_ADD(acc, b[off + i]);
+          acc = __shfl_sync(gmask, acc, 0, 8);
+        }
+        if (j == 0) heap[sh.id[L]] = acc;
+      }
     }
-    if (lane == 0) A.out[row] = A.mean ? np_mean_from_sum(BT_ADD(0.0f, total), n) : BT_ADD(0.0f, total);
-    __syncwarp();   // the heap is reused by the next row
+    __syncwarp();                     // the buffer is refilled two chunks later
+    if (c == nch - 1) {
+      float total;
+      if (perfect && D <= 9) {
+        const float* leaf = heap + (1 << D);
+        switch (D) {
+          case 9: total = dir_lane_leaves<16>(leaf + 16 * lane); break;
+          case 8: total = dir_lane_leaves<8>(leaf + 8 * lane); break;
+          case 7: total = dir_lane_leaves<4>(leaf + 4 * lane); break;
+          case 6: total = dir_lane_leaves<2>(leaf + 2 * lane); break;
+          default: total = lane < (1 << D) ? leaf[lane] : 0.0f; break;
+        }
+        const int levels = D < 5 ? D : 5;
+        for (int m = 0; m < levels; ++m) total = BT_ADD(total, __shfl_xor_sync(0xffffffffu, total, 1 << m));
+        total = __shfl_sync(0xffffffffu, total, 0);
+      } else {
+        for (int k = D - 1; k >= 0; --k) {
+          for (int jj = lane; jj < (1 << k); jj += 32) {
+            const int hh = (1 << k) + jj;
+            if ((sh.inner[hh >> 5] >> (hh & 31)) & 1u) heap[hh] = BT_ADD(heap[2 * hh], heap[2 * hh + 1]);
+          }
+          __syncwarp();
+        }
+        total = heap[1];
+      }
+      if (lane == 0) A.out[r] = A.mean ? np_mean_from_sum(BT_ADD(0.0f, total), n) : BT_ADD(0.0f, total);
+      __syncwarp();                   // the heap is reused by the next row
+    }
+    r = rn;
+    c = cn;
+    slot ^= 1;
   }
+  cp_async_wait_all();
+}
+
+// Runs of whole leaves spanning at most kChunk values, in row order.
+bool chunk_plan(const DPlan& p, uint16_t* chunk_leaf, int* n_chunk) {
+  int nc = 0, L = 0;
+  while (L < p.n_leaf) {
+    if (nc >= kDirLeaves) return false;
+    chunk_leaf[nc++] = (uint16_t)L;
+    const int start = p.off[L];
+    int L1 = L + 1;
+    while (L1 < p.n_leaf && (int)p.off[L1] + (int)p.len[L1] - start <= kChunk) ++L1;
+    L = L1;
+  }
+  chunk_leaf[nc] = (uint16_t)p.n_leaf;
+  *n_chunk = nc;
+  return true;
 }
 
 void dplan_node(DPlan& p, int h, int lo, int n, bool& ok) {
@@ -1115,7 +1180,7 @@ void dplan_node(DPlan& p, int h, int lo, int n, bool& ok) {
   dplan_node(p, 2 * h + 1, lo + n2, n - n2, ok);
 }
 
-// The pairwise plan of a row of n values for dir_reduce_kernel (cached).
+// The pairwise plan of a row of n values for chunk_reduce_kernel (cached).
 bool dplan_for(int n, DPlan* out) {
   if (n < 1 || n > kMaxRow) return false;
   static std::mutex mu;
@@ -1271,18 +1336,36 @@ extern "C" int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int 
   }
   cudaStream_t s = cur_stream();
   if (I == 1 && x->dtype == BT_F32 && R > kWarpRowMax) {
-    // rows too long for a warp's shared-memory slice: read them straight
-    // from global memory, one warp per row (shorter rows stage through
-    // shared memory, whose coalesced copies measured faster)
+    // rows too long for a warp's shared-memory slice: streamed through two
+    // chunk buffers per warp (shorter rows stage whole, which measured
+    // faster at 2048 values)
     DPlan dp;
     DevInfo di;
     if ((rc = dev_info(&di))) return rc;
-    if (O >= 2ll * di.sm_count * 8 && R <= kMaxRow && dplan_for((int)R, &dp)) {
-      DReduceArgs a{dp, (const float*)x->data, kind == BT_REDUCE_MEAN, O, (float*)out->data};
+    CReduceArgs ca;   // the kernel parameter block (about 3 KB)
+    if (O >= 4ll * di.sm_count && R <= kMaxRow && dplan_for((int)R, &dp) &&
+        chunk_plan(dp, ca.chunk_leaf, &ca.n_chunk)) {
+      ca.P = dp;
+      ca.x = (const float*)x->data;
+      ca.mean = kind == BT_REDUCE_MEAN;
+      ca.rows = O;
+      ca.out = (float*)out->data;
+      const size_t smem = (size_t)8 * chunk_warp_floats(dp.D) * sizeof(float);
+      static std::atomic<int> attr_done[kMaxDevices];
+      if (di.device >= kMaxDevices) return set_error(BT_EUNSUPPORTED, "device ordinal %d", di.device);
+      if (!attr_done[di.device].load()) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, chunk_reduce_kernel);
+        if (e == cudaSuccess)
+          e = cudaFuncSetAttribute(chunk_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   di.max_smem_optin - (int)fa.sharedSizeBytes);
+        if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_reduce(chunked rows) attributes: %s", cudaGetErrorString(e));
+        attr_done[di.device].store(1);
+      }
       int64_t g = (O + 7) / 8;
       if (g > 2147483647) g = 2147483647;
-      dir_reduce_kernel<<<(int)g, 256, (size_t)8 * (2 << dp.D) * sizeof(float), s>>>(a);
-      return check_launch("bt_reduce(direct rows)");
+      chunk_reduce_kernel<<<(int)g, 256, smem, s>>>(ca);
+      return check_launch("bt_reduce(chunked rows)");
     }
   }
   if (I == 1) {

@@ -269,3 +269,29 @@ def test_cuda_graph_replay_matches_eager(lib):
     torch.cuda.synchronize()
     for n in S.stage_outputs():
         assert_same(dec.out[n], want[n], n)
+
+
+def test_host_pipeline_matches_run_host(lib):
+    """The overlapped host-buffer loop (HostPipeline: copies on side streams,
+    ordered by events against the compute stream) returns, after several
+    steps, exactly what the serial FusedDecoder.run_host returns."""
+    from bt_b200.decoder import build_stream, FusedDecoder, fill_conv_standins, host_inputs, load_host_inputs
+    S = build_stream(3, t0=40)
+    dec = FusedDecoder(S)
+    fill_conv_standins(dec, seed=11)
+    load_host_inputs(dec, host_inputs(S, seed=12))
+    hin, hout = dec.host_buffers()
+    feat = S.stages[0].x_in
+    hin[feat].copy_(dec.inputs[feat].cpu())
+    for i, fc in enumerate(dec.fc_bufs):
+        hin[f"fc{i}"].copy_(fc.cpu())
+    dec.run_host(hin, hout)
+    torch.cuda.synchronize()
+    want = hout.clone()
+    hout.zero_()
+    pipe = dec.host_pipeline(hin, hout)
+    for _ in range(4):
+        pipe.step()
+    pipe.finish()
+    torch.cuda.synchronize()
+    assert torch.equal(hout.view(torch.int32), want.view(torch.int32))
