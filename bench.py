@@ -337,6 +337,19 @@ def per_op(rt, torch, peak):
     osw = [torch.empty_like(A3)]
     ms, gbs = measure_op(lambda: rt.adain_snake([A3], gsw, gsw, 1e-5, outs=osw), 2 * n * 4, flush, 5, torch)
     sweep["adain_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    # AdaIN + Snake whose output feeds DynamicQuantizeLinear, the range pass
+    # separate (adain, range, quantize) and folded into the AdaIN kernel
+    # (adain + range, quantize); algorithmic bytes of the pair: x read,
+    # the Snake output written and read back once, y written
+    al3 = (torch.rand(128, device="cuda") + 0.5).half()
+    ial3 = (1.0 / al3.float()).half()
+    rec3 = rt.range_records(1)
+    for nm, fused in (("adain_snake_dynquant_separate", False), ("adain_snake_dynquant_fused", True)):
+        def pair(fused=fused):
+            rt.adain_snake([A3], gsw, gsw, 1e-5, al3, ial3, outs=osw, ranges=rec3 if fused else None)
+            rt.dynamic_quantize(osw[0], range=rec3[0] if fused else None)
+        ms, gbs = measure_op(pair, 13 * n, flush, 5, torch)
+        sweep[nm] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt._reduce_block(A3, [2], 1), n * 4, flush, 5, torch)
     sweep["reducemean_8192"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt.dynamic_quantize(A), 5 * n + 5, flush, 5, torch)

@@ -89,6 +89,7 @@ SIGNATURES = {
     "bt_layernorm": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), _P(BtTensor), _P(BtTensor), _P(BtTensor),
                                     ctypes.c_int, ctypes.c_float, _P(BtTensor)]),
     "bt_adain_snake": (ctypes.c_int, [_P(BtAdainArgs)]),
+    "bt_adain_snake_range": (ctypes.c_int, [_P(BtAdainArgs), ctypes.c_void_p]),
     "bt_resblock_mean_leaky": (ctypes.c_int, [_P(ctypes.c_void_p), _P(ctypes.c_void_p), ctypes.c_int64,
                                               ctypes.c_float, ctypes.c_float, ctypes.c_void_p]),
     "bt_plan_broadcast": (ctypes.c_int, [ctypes.c_int, _P(BtTensor), _P(ctypes.c_int64), ctypes.c_int,
@@ -97,6 +98,8 @@ SIGNATURES = {
     "bt_selfcheck": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]),
     "bt_dynamic_quantize": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
     "bt_dynamic_quantize_noalloc": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
+    "bt_dynamic_quantize_ranged": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_void_p]),
     "bt_conv_int_epilogue": (ctypes.c_int, [_P(BtTensor)] * 5),
 }
 

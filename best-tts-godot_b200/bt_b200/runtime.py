@@ -453,18 +453,25 @@ class BtRuntime:
             v = info.min if low else info.max
         return torch.tensor(np.array(v, dtype=dt)).to(self.device)
 
-    def dynamic_quantize(self, x):
+    def dynamic_quantize(self, x, range=None):
         """DynamicQuantizeLinear of a float32 / float16 tensor
         (bt_dynamic_quantize): (y uint8 of x's shape, scale float32 0-d,
-        zero point uint8 0-d)."""
+        zero point uint8 0-d).  range: x's range record as its producer
+        wrote it (adain_snake(..., ranges=)); only the quantize pass runs
+        then (bt_dynamic_quantize_ranged)."""
         x = self._contig(x)
         y = self._empty(tuple(x.shape), np.uint8)
         sc = self._empty((), np.float32)
         zp = self._empty((), np.uint8)
         self._stream()
-        check(self.lib.bt_dynamic_quantize(tensor_desc(x), tensor_desc(y), sc.data_ptr(), zp.data_ptr()),
-              "bt_dynamic_quantize")
-        self.launches += 2
+        if range is None:
+            check(self.lib.bt_dynamic_quantize(tensor_desc(x), tensor_desc(y), sc.data_ptr(), zp.data_ptr()),
+                  "bt_dynamic_quantize")
+            self.launches += 2
+        else:
+            check(self.lib.bt_dynamic_quantize_ranged(tensor_desc(x), tensor_desc(y), sc.data_ptr(), zp.data_ptr(),
+                                                      range.data_ptr()), "bt_dynamic_quantize_ranged")
+            self.launches += 1
         return y, sc, zp
 
     def conv_int_epilogue(self, acc, bias, x_scale, w_scale):
@@ -611,10 +618,14 @@ class BtRuntime:
         shape2 = np.broadcast_shapes(shape, tuple(gain.shape))
         return self.elementwise("MUL", [d, self._as_f32(gain)], shape2, np.float32, np.float32)
 
-    def adain_snake(self, srcs, gain, shift, eps, alpha=None, inv_alpha=None, res=None, outs=None):
+    def adain_snake(self, srcs, gain, shift, eps, alpha=None, inv_alpha=None, res=None, outs=None,
+                    ranges=None):
         """Row-fused AdaIN1d (+ Snake) of [B, C, T] float32 tensors (see
         bt_adain_snake in bt_ops.h).  gain / shift are [B, C] float32 views
-        with unit channel stride; alpha / inv_alpha [C] (fp16 or fp32)."""
+        with unit channel stride; alpha / inv_alpha [C] (fp16 or fp32).
+        ranges: an int32 device tensor of 4 words per output; when given,
+        bt_adain_snake_range also records each output's value range there
+        for dynamic_quantize(out, range=ranges[k])."""
         x0 = srcs[0]
         B, Cc, T = x0.shape
         a = _lib.BtAdainArgs()
@@ -646,9 +657,17 @@ class BtRuntime:
                 a.inv_alpha[i] = invs[i].data_ptr()
             a.out[i] = outs[i].data_ptr()
         self._stream()
-        check(self.lib.bt_adain_snake(ctypes.byref(a)), "bt_adain_snake")
+        if ranges is None:
+            check(self.lib.bt_adain_snake(ctypes.byref(a)), "bt_adain_snake")
+        else:
+            assert ranges.is_contiguous() and ranges.numel() >= 4 * len(gains) and ranges.element_size() == 4
+            check(self.lib.bt_adain_snake_range(ctypes.byref(a), ranges.data_ptr()), "bt_adain_snake_range")
         self.launches += 1
         return outs
+
+    def range_records(self, n):
+        """Device storage for n range records (bt_adain_snake_range)."""
+        return torch.empty((n, 4), dtype=torch.int32, device=self.device)
 
     def _fit_param(self, p, trailing):
         """gamma/beta as a contiguous run over the normalised axes (broadcast

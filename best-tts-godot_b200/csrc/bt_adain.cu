@@ -77,6 +77,7 @@ struct AdainArgs {
   const void* alpha[BT_ADAIN_MAX_OUT];
   const void* inv_alpha[BT_ADAIN_MAX_OUT];
   float* out[BT_ADAIN_MAX_OUT];
+  uint32_t* range[BT_ADAIN_MAX_OUT];     // RANGE kernels: output k's min / max / NaN record
 };
 
 __device__ __forceinline__ int phase4(const void* p) { return (int)(((uintptr_t)p >> 2) & 3); }
@@ -260,7 +261,17 @@ __device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0,
   }
 }
 
-template <int NSRC, bool SNAKE>
+// Order-preserving map of non-NaN floats to unsigned integers (the range
+// record of bt_dynamic_quantize: [0] = ~ord(min) and [1] = ord(max) by
+// atomicMax, [2] = NaN seen; all three start at 0).
+__device__ __forceinline__ uint32_t range_ord(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// RANGE: also folds every output value into that output's range record
+// (DynamicQuantizeLinear of the output then needs no pass of its own over it).
+template <int NSRC, bool SNAKE, bool RANGE = false>
 __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float prm[BT_ADAIN_MAX_OUT][4];   // gain, shift, alpha, 1/alpha of this row
@@ -420,22 +431,69 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
         y = pk_add_lanes(y, pk_mul(pk(ial), pk_np_sin<true, decltype(checked)::value>(pk_mul(pk(al), y))));
       return y;
     };
+    // the range of the values written (RANGE)
+    float rlo = INFINITY, rhi = -INFINITY;
+    bool rnan = false;
+    auto track = [&](float v) {
+      if (RANGE) {
+        rnan |= v != v;
+        rlo = fminf(rlo, v);
+        rhi = fmaxf(rhi, v);
+      }
+    };
     auto vec_loop = [&](float* o, auto checked) {
 #pragma unroll 2
       for (int q = threadIdx.x; q < nvec; q += kThreads) {
         const float4 v = *(const float4*)(b0 + head + 4 * q);
         const float2 lo = f2(pk(v.x, v.y), checked), hi = f2(pk(v.z, v.w), checked);
         __stcs((float4*)(o + head + 4 * q), make_float4(lo.x, lo.y, hi.x, hi.y));
+        track(lo.x); track(lo.y); track(hi.x); track(hi.y);
       }
+    };
+    auto put = [&](float* o, int i) {
+      const float v = f(b0[i]);
+      o[i] = v;
+      track(v);
     };
     float* o = A.out[k] + gofs;
     if (phase4(o) == phase4(g0)) {
       if (SNAKE && in_range[k]) vec_loop(o, std::false_type());
       else vec_loop(o, std::true_type());
-      for (int i = threadIdx.x; i < head; i += kThreads) o[i] = f(b0[i]);
-      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) o[i] = f(b0[i]);
+      for (int i = threadIdx.x; i < head; i += kThreads) put(o, i);
+      for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) put(o, i);
     } else {
-      for (int i = threadIdx.x; i < seg; i += kThreads) o[i] = f(b0[i]);
+      for (int i = threadIdx.x; i < seg; i += kThreads) put(o, i);
+    }
+    if (RANGE) {
+      // CTA-wide min / max / NaN of this output, one atomic each per CTA
+      __shared__ float sr_lo[kThreads / 32], sr_hi[kThreads / 32];
+      __shared__ int sr_nan;
+      for (int m = 16; m > 0; m >>= 1) {
+        rlo = fminf(rlo, __shfl_xor_sync(0xffffffffu, rlo, m));
+        rhi = fmaxf(rhi, __shfl_xor_sync(0xffffffffu, rhi, m));
+      }
+      rnan = __any_sync(0xffffffffu, rnan);
+      if (threadIdx.x == 0) sr_nan = 0;
+      __syncthreads();
+      if ((threadIdx.x & 31) == 0) {
+        sr_lo[threadIdx.x >> 5] = rlo;
+        sr_hi[threadIdx.x >> 5] = rhi;
+        if (rnan) sr_nan = 1;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int w = 1; w < kThreads / 32; ++w) {
+          rlo = fminf(rlo, sr_lo[w]);
+          rhi = fmaxf(rhi, sr_hi[w]);
+        }
+        uint32_t* rec = A.range[k];
+        if (rlo <= rhi) {   // not an all-NaN (or empty) segment
+          atomicMax(&rec[0], ~range_ord(rlo));
+          atomicMax(&rec[1], range_ord(rhi));
+        }
+        if (sr_nan) atomicOr(&rec[2], 1u);
+      }
+      __syncthreads();   // the shared words are reused by the next output
     }
   }
 }
@@ -574,18 +632,22 @@ const ClusterPlan& cluster_plan(int T, int cs) {
   return cache.emplace(key, cp).first->second;
 }
 
-template <int NSRC, bool SNAKE>
-void* kernel_ptr() { return (void*)adain_cluster_kernel<NSRC, SNAKE>; }
+template <int NSRC, bool SNAKE, bool RANGE>
+void* kernel_ptr() { return (void*)adain_cluster_kernel<NSRC, SNAKE, RANGE>; }
 
-void* pick_kernel(int nsrc, bool snake) {
+template <bool RANGE>
+void* pick_kernel_t(int nsrc, bool snake) {
   switch (nsrc * 2 + (snake ? 1 : 0)) {
-    case 2: return kernel_ptr<1, false>();
-    case 3: return kernel_ptr<1, true>();
-    case 4: return kernel_ptr<2, false>();
-    case 5: return kernel_ptr<2, true>();
-    case 6: return kernel_ptr<3, false>();
-    default: return kernel_ptr<3, true>();
+    case 2: return kernel_ptr<1, false, RANGE>();
+    case 3: return kernel_ptr<1, true, RANGE>();
+    case 4: return kernel_ptr<2, false, RANGE>();
+    case 5: return kernel_ptr<2, true, RANGE>();
+    case 6: return kernel_ptr<3, false, RANGE>();
+    default: return kernel_ptr<3, true, RANGE>();
   }
+}
+void* pick_kernel(int nsrc, bool snake, bool range = false) {
+  return range ? pick_kernel_t<true>(nsrc, snake) : pick_kernel_t<false>(nsrc, snake);
 }
 
 std::mutex g_attr_mu;
@@ -600,9 +662,9 @@ int set_attributes(int device, int max_smem, size_t* dyn_max) {
   if (device < 0 || device >= 64) return set_error(BT_EUNSUPPORTED, "device ordinal %d", device);
   if (!g_attr_done[device]) {
     size_t lim = (size_t)max_smem;
-    for (int ns = 1; ns <= 3; ++ns)
-      for (int sn = 0; sn < 2; ++sn) {
-        void* fn = pick_kernel(ns, sn != 0);
+    for (int v = 0; v < 12; ++v) {
+        const int ns = 1 + v % 3, sn = (v / 3) % 2, rg = v / 6;
+        void* fn = pick_kernel(ns, sn != 0, rg != 0);
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, fn);
         if (e != cudaSuccess) return set_error(BT_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
@@ -623,7 +685,9 @@ int set_attributes(int device, int max_smem, size_t* dyn_max) {
 
 // Launches the cluster kernel; returns BT_EUNSUPPORTED when this request is
 // outside what it handles (the caller then uses the one-CTA-per-row kernel).
-int adain_v3(const bt_adain_args* p) {
+// range (optional): per output, a zeroed 3-word min / max / NaN record that
+// the kernel folds the written values into.
+int adain_v3(const bt_adain_args* p, uint32_t* const* range) {
   const char* env = getenv("BT_ADAIN_ONE_CTA");
   if (env && env[0] == '1') return BT_EUNSUPPORTED;
   if (p->cols < 1 || p->cols > kMaxT) return BT_EUNSUPPORTED;
@@ -683,6 +747,7 @@ int adain_v3(const bt_adain_args* p) {
     A.alpha[k] = p->alpha[k];
     A.inv_alpha[k] = p->inv_alpha[k];
     A.out[k] = p->out[k];
+    A.range[k] = range ? range[k] : nullptr;
   }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
@@ -698,7 +763,7 @@ int adain_v3(const bt_adain_args* p) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   void* args[] = {(void*)&A};
-  cudaError_t e = cudaLaunchKernelExC(&cfg, pick_kernel(p->n_src, snake), args);
+  cudaError_t e = cudaLaunchKernelExC(&cfg, pick_kernel(p->n_src, snake, range != nullptr), args);
   if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_adain_snake(cluster): %s", cudaGetErrorString(e));
   return check_launch("bt_adain_snake(cluster)");
 }

@@ -47,7 +47,15 @@ int plan_broadcast(int n_ops, const bt_tensor* const* ops,
 
 // AdaIN1d + Snake with rows split across a thread-block cluster (bt_adain.cu).
 // Returns BT_EUNSUPPORTED, without setting an error, for requests it does
-// not cover; bt_adain_snake then uses the one-CTA-per-row kernel.
-int adain_v3(const bt_adain_args* p);
+// not cover; bt_adain_snake then uses the one-CTA-per-row kernel.  range
+// (may be null): per output a zeroed 3-word record ([0] = ~ord(min) and
+// [1] = ord(max), both by atomicMax, [2] = NaN seen) that the kernel folds
+// every written value into -- the record dq_range_launch fills.
+int adain_v3(const bt_adain_args* p, uint32_t* const* range = nullptr);
+
+// The range pass of DynamicQuantizeLinear (bt_quant.cu) over n contiguous
+// values of x (float32 or float16) into a zeroed 3-word record, on the
+// current stream.
+int dq_range_launch(const void* x, int32_t dtype, int64_t n, uint32_t* rec);
 
 }  // namespace bt

@@ -199,6 +199,27 @@ int scratch_for(int device, cudaStream_t s, uint32_t** out) {
 
 }  // namespace
 
+// The quantize pass over a filled range record.
+int dq_quantize_launch(const bt_tensor* x, const bt_tensor* y, float* scale_out, uint8_t* zp_out,
+                       const uint32_t* rec, const char* what) {
+  const int64_t n = numel(x);
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  int64_t blocks = (n + kThreads * 16 - 1) / (kThreads * 16);
+  const int64_t cap = (int64_t)di.sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  cudaStream_t s = cur_stream();
+  if (x->dtype == BT_F32)
+    dq_quantize_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, rec, (uint8_t*)y->data,
+                                                               scale_out, zp_out);
+  else
+    dq_quantize_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, rec, (uint8_t*)y->data,
+                                                                scale_out, zp_out);
+  return check_launch(what);
+}
+
 // Shared by bt_dynamic_quantize and its no-allocation variant: the launches
 // over a given scratch record.
 int dynamic_quantize_run(const bt_tensor* x, const bt_tensor* y, float* scale_out, uint8_t* zp_out,
@@ -214,16 +235,22 @@ int dynamic_quantize_run(const bt_tensor* x, const bt_tensor* y, float* scale_ou
   const int64_t cap = (int64_t)di.sm_count * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  if (x->dtype == BT_F32) {
-    dq_range_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, scratch);
-    dq_quantize_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, scratch, (uint8_t*)y->data,
-                                                               scale_out, zp_out);
-  } else {
-    dq_range_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, scratch);
-    dq_quantize_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, scratch,
-                                                                (uint8_t*)y->data, scale_out, zp_out);
-  }
-  return check_launch("bt_dynamic_quantize");
+  if (x->dtype == BT_F32) dq_range_kernel<float><<<(int)blocks, kThreads, 0, s>>>((const float*)x->data, n, scratch);
+  else dq_range_kernel<__half><<<(int)blocks, kThreads, 0, s>>>((const __half*)x->data, n, scratch);
+  return dq_quantize_launch(x, y, scale_out, zp_out, scratch, "bt_dynamic_quantize");
+}
+
+int dq_range_launch(const void* x, int32_t dtype, int64_t n, uint32_t* rec) {
+  DevInfo di;
+  int rc = dev_info(&di);
+  if (rc) return rc;
+  int64_t blocks = (n + kThreads * 16 - 1) / (kThreads * 16);
+  const int64_t cap = (int64_t)di.sm_count * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  if (dtype == BT_F32) dq_range_kernel<float><<<(int)blocks, kThreads, 0, cur_stream()>>>((const float*)x, n, rec);
+  else dq_range_kernel<__half><<<(int)blocks, kThreads, 0, cur_stream()>>>((const __half*)x, n, rec);
+  return check_launch("dq_range");
 }
 
 int dynamic_quantize_check(const bt_tensor* x, const bt_tensor* y, const float* scale_out, const uint8_t* zp_out,
@@ -308,4 +335,17 @@ extern "C" int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* 
   uint32_t* scratch = nullptr;
   if ((rc = noalloc_scratch(di.device, &scratch))) return rc;
   return dynamic_quantize_run(x, y, scale_out, zp_out, scratch);
+}
+
+// ---- DynamicQuantizeLinear over a range its producer recorded ----------------
+// bt_adain_snake_range folds each output's values into a range record as it
+// writes them; the quantization of that output then only needs the second
+// pass.  The record is the one the range kernel above fills, so the results
+// are those of bt_dynamic_quantize bit for bit.
+extern "C" int bt_dynamic_quantize_ranged(const bt_tensor* x, const bt_tensor* y, float* scale_out, uint8_t* zp_out,
+                                          const uint32_t* range) {
+  int rc = dynamic_quantize_check(x, y, scale_out, zp_out, "bt_dynamic_quantize_ranged");
+  if (rc) return rc;
+  if (!range) return set_error(BT_EINVAL, "bt_dynamic_quantize_ranged: null range record");
+  return dq_quantize_launch(x, y, scale_out, zp_out, range, "bt_dynamic_quantize_ranged");
 }

@@ -1524,7 +1524,9 @@ extern "C" int bt_layernorm(const bt_tensor* x, const bt_tensor* skip, const bt_
   return check_launch("bt_layernorm");
 }
 
-extern "C" int bt_adain_snake(const bt_adain_args* p) {
+namespace {
+
+int adain_check(const bt_adain_args* p) {
   if (!p) return set_error(BT_EINVAL, "bt_adain_snake: null argument");
   if (p->rows < 0 || p->cols < 1 || p->channels < 1)
     return set_error(BT_EINVAL, "bt_adain_snake: rows %lld cols %lld channels %lld", (long long)p->rows,
@@ -1544,9 +1546,11 @@ extern "C" int bt_adain_snake(const bt_adain_args* p) {
   if (p->gain_stride < p->channels || p->shift_stride < p->channels)
     return set_error(BT_EINVAL, "bt_adain_snake: gain/shift batch strides (%lld, %lld) below C = %lld",
                      (long long)p->gain_stride, (long long)p->shift_stride, (long long)p->channels);
-  if (p->rows == 0) return BT_OK;
-  const int rc3 = adain_v3(p);
-  if (rc3 != BT_EUNSUPPORTED) return rc3;
+  return BT_OK;
+}
+
+// the one-CTA-per-row kernel
+int adain_one_cta(const bt_adain_args* p) {
   if (p->cols > kMaxRow) return set_error(BT_ETOOBIG, "bt_adain_snake: rows of %lld values exceed %d", (long long)p->cols, kMaxRow);
   size_t smem;
   int depth, rc;
@@ -1557,6 +1561,36 @@ extern "C" int bt_adain_snake(const bt_adain_args* p) {
   A.n = (int)p->cols;
   adain_snake_kernel<<<row_grid(p->rows), row_threads((int)p->cols), smem, cur_stream()>>>(A);
   return check_launch("bt_adain_snake");
+}
+
+}  // namespace
+
+extern "C" int bt_adain_snake(const bt_adain_args* p) {
+  int rc = adain_check(p);
+  if (rc) return rc;
+  if (p->rows == 0) return BT_OK;
+  rc = adain_v3(p);
+  if (rc != BT_EUNSUPPORTED) return rc;
+  return adain_one_cta(p);
+}
+
+extern "C" int bt_adain_snake_range(const bt_adain_args* p, uint32_t* range) {
+  int rc = adain_check(p);
+  if (rc) return rc;
+  if (!range) return set_error(BT_EINVAL, "bt_adain_snake_range: null range records");
+  if ((uintptr_t)range & 15) return set_error(BT_EINVAL, "bt_adain_snake_range: range records not 16-byte aligned");
+  cudaError_t e = cudaMemsetAsync(range, 0, (size_t)16 * p->n_out, cur_stream());
+  if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_adain_snake_range: memset: %s", cudaGetErrorString(e));
+  if (p->rows == 0) return BT_OK;
+  uint32_t* rec[BT_ADAIN_MAX_OUT];
+  for (int k = 0; k < p->n_out; ++k) rec[k] = range + 4 * k;
+  rc = adain_v3(p, rec);
+  if (rc != BT_EUNSUPPORTED) return rc;
+  // outside the cluster kernel: the one-CTA kernel, then a range pass per output
+  if ((rc = adain_one_cta(p))) return rc;
+  for (int k = 0; k < p->n_out; ++k)
+    if ((rc = dq_range_launch(p->out[k], BT_F32, p->rows * p->cols, rec[k]))) return rc;
+  return BT_OK;
 }
 
 extern "C" int bt_resblock_mean_leaky(const float* const* a, const float* const* b, int64_t n, float divisor,

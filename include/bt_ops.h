@@ -210,6 +210,17 @@ typedef struct bt_adain_args {
   float*       out[BT_ADAIN_MAX_OUT];    /* [R, T] fp32 */
 } bt_adain_args;
 int bt_adain_snake(const bt_adain_args* a);
+/* bt_adain_snake whose outputs go on to a DynamicQuantizeLinear (the input
+ * quantisation of the ConvInteger that reads each Snake output in the int8
+ * generator): the same outputs, bit for bit, and in the same pass output k's
+ * values folded into the range record range + 4 * k, which
+ * bt_dynamic_quantize_ranged then consumes.  range: device memory, 16-byte
+ * aligned, 16 bytes per output; this call zeroes the records first.  Where
+ * the cluster kernel does not apply it runs a separate range pass per output
+ * instead, with the same records as the result.
+ * replaces: the minmax dispatch of executor.gd:1224-1230 (its pass over the
+ *           Snake output) for each quantised conv input. */
+int bt_adain_snake_range(const bt_adain_args* a, uint32_t* range);
 
 /* ---- residual mean + LeakyRelu (end of a generator stage) ---------------
  * out = leaky((((a0 + b0) + (a1 + b1)) + (a2 + b2)) / 3, slope) elementwise
@@ -251,6 +262,15 @@ int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out
  * its min/max scratch (executor.gd:1201-1206). */
 int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* y,
                                 float* scale_out, uint8_t* zp_out);
+/* bt_dynamic_quantize of an x whose range record its producer already wrote
+ * (bt_adain_snake_range): only the quantize pass runs, results identical to
+ * bt_dynamic_quantize's.  range points at the 16-byte record of x, left
+ * unchanged.
+ * replaces: the quantize dispatch of executor.gd:1232-1238 after a fused
+ *           minmax. */
+int bt_dynamic_quantize_ranged(const bt_tensor* x, const bt_tensor* y,
+                               float* scale_out, uint8_t* zp_out,
+                               const uint32_t* range);
 
 /* ---- integer convolution epilogue ----------------------------------------
  * The nodes after each ConvInteger of the quantised generator in one pass:

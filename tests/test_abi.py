@@ -51,6 +51,17 @@ def test_errors_set_message(lib):
     args.n_src = 1
     assert lib.bt_adain_snake(ctypes.byref(args)) == -1     # src[0] null
     assert b"src[0]" in lib.bt_last_error()
+    assert lib.bt_adain_snake_range(ctypes.byref(args), ctypes.c_void_p(16)) == -1     # validated first
+    assert b"src[0]" in lib.bt_last_error()
+    args.src[0] = args.out[0] = args.gain[0] = args.shift[0] = 16
+    args.gain_stride = args.shift_stride = 2
+    args.alpha_dtype = _lib.BT_F32
+    assert lib.bt_adain_snake_range(ctypes.byref(args), None) == -1
+    assert b"null range" in lib.bt_last_error()
+    assert lib.bt_adain_snake_range(ctypes.byref(args), ctypes.c_void_p(20)) == -1
+    assert b"16-byte" in lib.bt_last_error()
+    y = _lib.make_tensor(0, np.uint8, (4,))
+    assert lib.bt_dynamic_quantize_ranged(ctypes.byref(x), ctypes.byref(y), None, None, None) == -1
     assert lib.bt_selfcheck(6, 0, 16, None) == -1 and b"kind" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 0, 16, None) == -1 and b"null" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 1, 1 << 32, ctypes.c_void_p(16)) == -1
