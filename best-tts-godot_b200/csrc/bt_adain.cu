@@ -28,6 +28,7 @@
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
+#include "bt_dq.h"
 #include "bt_pk.h"
 
 namespace bt {
@@ -261,14 +262,6 @@ __device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0,
   }
 }
 
-// Order-preserving map of non-NaN floats to unsigned integers (the range
-// record of bt_dynamic_quantize: [0] = ~ord(min) and [1] = ord(max) by
-// atomicMax, [2] = NaN seen; all three start at 0).
-__device__ __forceinline__ uint32_t range_ord(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 // RANGE: also folds every output value into that output's range record
 // (DynamicQuantizeLinear of the output then needs no pass of its own over it).
 template <int NSRC, bool SNAKE, bool RANGE = false>
@@ -488,8 +481,8 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
         }
         uint32_t* rec = A.range[k];
         if (rlo <= rhi) {   // not an all-NaN (or empty) segment
-          atomicMax(&rec[0], ~range_ord(rlo));
-          atomicMax(&rec[1], range_ord(rhi));
+          atomicMax(&rec[0], ~dq_ord(rlo));
+          atomicMax(&rec[1], dq_ord(rhi));
         }
         if (sr_nan) atomicOr(&rec[2], 1u);
       }

@@ -12,7 +12,9 @@
 // order-preserving integers, all identities 0, so one memset clears it); the
 // second has every CTA derive scale and zero point from the record -- the
 // same double arithmetic in every CTA, so all agree -- and quantizes 16
-// values per thread (four 128-bit loads, one 128-bit store).  CTA 0 writes
+// values per thread (four 128-bit loads, one 128-bit store), each by a
+// float32 shortcut that falls back to the exact double quotient near the
+// half-integers where the two could differ (bt_dq.h).  CTA 0 writes
 // the scale and zero-point outputs.  A NaN anywhere makes numpy's min and max
 // NaN, which Python's min(0.0, nan) and max(0.0, nan) turn into 0: scale 1,
 // zero point 0; the NaN elements themselves become 0 here (numpy's cast of
@@ -26,20 +28,12 @@
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
+#include "bt_dq.h"
 
 namespace bt {
 namespace {
 
 constexpr int kThreads = 256;
-
-// Order-preserving map of non-NaN floats to unsigned integers.
-__device__ __forceinline__ uint32_t ord_bits(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float from_ord(uint32_t o) {
-  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-}
 
 // scratch[0] = ~ord(min) (atomicMax), scratch[1] = ord(max), scratch[2] = NaN seen
 template <typename T>
@@ -104,45 +98,11 @@ __global__ void __launch_bounds__(kThreads) dq_range_kernel(const T* x, int64_t 
     }
     // an all-NaN share leaves lo = +inf, hi = -inf: the identities
     if (lo <= hi) {
-      atomicMax(&scratch[0], ~ord_bits(lo));
-      atomicMax(&scratch[1], ord_bits(hi));
+      atomicMax(&scratch[0], ~dq_ord(lo));
+      atomicMax(&scratch[1], dq_ord(hi));
     }
     if (snan) atomicOr(&scratch[2], 1u);
   }
-}
-
-struct DqParams {
-  float scale32;   // float32(scale): the divisor of the element quotients
-  float zp;        // zero point, integral in [0, 255]
-  double rscale;   // recip_d(scale32)
-};
-
-// scale and zero point from the range record (every CTA, identically)
-__device__ __forceinline__ DqParams dq_params(const uint32_t* scratch, int64_t n) {
-  double lo = 0.0, hi = 0.0;
-  if (scratch[2] == 0u && n > 0) {
-    const float m = from_ord(~scratch[0]), M = from_ord(scratch[1]);
-    if (m < 0.0f) lo = (double)m;     // min(0.0, float(m)) keeps 0.0 unless m < 0
-    if (M > 0.0f) hi = (double)M;     // max(0.0, float(M)) keeps 0.0 unless M > 0
-  }
-  double scale = __ddiv_rn(__dsub_rn(hi, lo), 255.0);
-  if (scale == 0.0) scale = 1.0;
-  double z = rint(__dsub_rn(0.0, __ddiv_rn(lo, scale)));
-  z = z != z ? 0.0 : fmin(fmax(z, 0.0), 255.0);
-  DqParams p;
-  p.scale32 = __double2float_rn(scale);
-  p.zp = (float)z;
-  p.rscale = recip_d(p.scale32);
-  return p;
-}
-
-__device__ __forceinline__ uint32_t q8(float x, const DqParams& p) {
-  // rint(x / scale) in float32 (the quotient by recip_d / div_by is the
-  // correctly rounded one), + zp (exact for |q| < 2^24; beyond that either
-  // way saturates), clip, NaN -> 0
-  const float v = BT_ADD(rintf(div_by(x, p.rscale)), p.zp);
-  if (!(v > 0.0f)) return 0u;
-  return v >= 255.0f ? 255u : (uint32_t)v;
 }
 
 template <typename T>

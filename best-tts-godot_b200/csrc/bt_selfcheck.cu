@@ -1,12 +1,14 @@
 // bt_selfcheck.cu -- exhaustive device checks of the library's own float32
 // math: the fast division inside exp and sigmoid, the double reciprocal
-// behind division by a per-row constant, and tanh (bt_selfcheck in bt_ops.h).
+// behind division by a per-row constant, tanh, and DynamicQuantizeLinear's
+// float32 shortcut (bt_selfcheck in bt_ops.h).
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
 #include "bt_pk.h"
+#include "bt_dq.h"
 
 namespace bt {
 namespace {
@@ -16,6 +18,10 @@ namespace {
 __device__ __forceinline__ bool same_bits(float a, float b) {
   return __float_as_uint(a) == __float_as_uint(b) || (a != a && b != b);
 }
+
+// the (scale, zero point) pairs of kind 6
+__constant__ double c_dq_scale[8] = {1.0, 0.0173, 3.0 / 255.0, 0x1.fffffep-1, 1e-30, 0x1p-140, 2.6e36, 0x1.000002p+3};
+__constant__ double c_dq_zp[8] = {0.0, 128.0, 255.0, 3.0, 0.0, 17.0, 255.0, 200.0};
 
 __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first, uint64_t count,
                                                         unsigned long long* mismatches) {
@@ -51,6 +57,19 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
         bad += same_bits(g.y, np_sigmoidf_t<true>(-x)) ? 0 : 1;
         break;
       }
+      case 6: {
+        // DynamicQuantizeLinear's float32 shortcut against its exact double
+        // path, at scales that put every quotient regime in reach: unit
+        // (ties at every half-integer), ordinary, the smallest and largest
+        // scales a float32 range gives, a scale whose reciprocal rounds
+        // across a binade, and zero points at both ends
+#pragma unroll 1
+        for (int j = 0; j < 8; ++j) {
+          const DqParams p = dq_params_from(c_dq_scale[j], c_dq_zp[j]);
+          bad += q8(x, p) == q8_exact(x, p) ? 0 : 1;
+        }
+        break;
+      }
       default: {
         // within one double ulp of IEEE's 1/x; NaN for NaN
         const double y = recip_d(x), z = __ddiv_rn(1.0, (double)x);
@@ -72,7 +91,7 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
 using namespace bt;
 
 extern "C" int bt_selfcheck(int kind, uint32_t first, uint64_t count, unsigned long long* mismatches) {
-  if (kind < 0 || kind > 5) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
+  if (kind < 0 || kind > 6) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
   if (!mismatches) return set_error(BT_EINVAL, "bt_selfcheck: null counter");
   if (count > (1ull << 32) || (uint64_t)first + count > (1ull << 32))
     return set_error(BT_EINVAL, "bt_selfcheck: range past 2^32 bit patterns");

@@ -315,8 +315,10 @@ int bt_host_math(int kind, const float* in, float* out, int64_t n);
  * instance norms), which must lie within one double ulp of IEEE's 1/x and
  * equal it on zeros, infinities and NaN, 4 sigmoid two lanes at a time
  * (each input paired with its negation), 5 tanh, which counts as a mismatch
- * only when it is more than one float ulp from the correctly rounded tanh.
- * Asynchronous on the set stream.
+ * only when it is more than one float ulp from the correctly rounded tanh,
+ * 6 DynamicQuantizeLinear's float32 shortcut against its exact double path
+ * at eight built-in (scale, zero point) pairs (a mismatch per differing
+ * pair).  Asynchronous on the set stream.
  * No counterpart in the reference: over all 2^32 inputs it shows that the
  * library's fast division gives the IEEE quotient, hence numpy's result,
  * in every use. */

@@ -72,6 +72,27 @@ def test_halfway_quotients(gpu_runtime):
     _check(gpu_runtime, np.tile(v, 40), what="ties")
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_near_half_quotients(gpu_runtime, seed):
+    """Values whose quotient x / scale lies within a few float ulps of a
+    half-integer, at random scales: where the kernel's float32 shortcut
+    hands over to the exact quotient."""
+    rng = np.random.default_rng(100 + seed)
+    lo = float(np.float32(-rng.uniform(0.01, 50.0)))
+    hi = float(np.float32(rng.uniform(0.01, 50.0)))
+    s32 = np.float32((hi - lo) / 255.0)     # the oracle's scale (double, then float32)
+    k = rng.integers(-120, 120, 20_000).astype(np.float64)
+    base = ((k + 0.5) * np.float64(s32)).astype(np.float32)
+    steps = rng.integers(-4, 5, base.size)
+    x = base.copy()
+    for st in range(1, 5):
+        x = np.where(steps >= st, np.nextafter(x, np.float32(np.inf)), x)
+        x = np.where(steps <= -st, np.nextafter(x, np.float32(-np.inf)), x)
+    x = np.clip(x, np.float32(lo), np.float32(hi))
+    x = np.concatenate([[np.float32(lo), np.float32(hi)], x]).astype(np.float32)
+    _check(gpu_runtime, x, what=f"near-half seed {seed}")
+
+
 def test_non_finite(gpu_runtime):
     rng = np.random.default_rng(9)
     x = rng.standard_normal(50_000).astype(np.float32)

@@ -15,7 +15,9 @@ every float, the bound under which RN32(RN64(a * (1/b))) is RN32(a/b).
 Tanh is the library's own double evaluation; the check holds it within one
 float ulp of the correctly rounded tanh on every input (numpy's float32 tanh
 is within one ulp of that too, so the two stay within the 2-ulp bound of the
-op tests)."""
+op tests).  DynamicQuantizeLinear's float32 shortcut (a reciprocal product,
+with the exact double quotient near half-integers) must equal the exact path
+on every input at each of eight scales."""
 import ctypes
 
 import pytest
@@ -28,7 +30,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("kind,name", [(0, "exp"), (1, "exp, two lanes"), (2, "sigmoid"),
                                        (3, "double reciprocal of a row constant"), (4, "sigmoid, two lanes"),
-                                       (5, "tanh within one ulp of the correctly rounded value")])
+                                       (5, "tanh within one ulp of the correctly rounded value"),
+                                       (6, "quantize shortcut against the exact quotient")])
 def test_fast_division_equals_ieee_on_every_input(lib, kind, name):
     count = torch.zeros(1, dtype=torch.int64, device="cuda")
     _lib.check(lib.bt_selfcheck(kind, 0, 1 << 32, ctypes.c_void_p(count.data_ptr())), "bt_selfcheck")
