@@ -14,6 +14,14 @@ hand-written sm_100a kernel behind the C ABI of ``libbt_ops.so``.  numpy
 arrays found in ``env`` (constants, initializers) are copied to the device on
 first use and cached; the caller's ``env`` entries are never replaced.
 
+Memory layout follows numpy too, because numpy's summation order depends on
+it: ``Transpose`` returns a permuted view (ref_runtime.py:517-518 returns
+``np.transpose``'s view), element-wise results are allocated in numpy's
+order 'K' (the axis order numpy's iterator picks from the operands'
+strides), uploads keep a numpy array's axis order, and a reduction over a
+view sums in the order numpy's iterator walks that view (pairwise along the
+innermost axis in memory, slice after slice along outer ones).
+
 Result dtypes and shapes follow numpy exactly: they are obtained by applying
 the same numpy expression to zero-size arrays of the operands' dtypes, and
 numpy's broadcasting rule.  Errors numpy would raise (bad broadcast, bad
@@ -114,8 +122,16 @@ class BtRuntime:
         hit = self._consts.get(key)
         if hit is not None and hit[0]() is v:
             return hit[1]
-        # (np.ascontiguousarray makes 0-d arrays 1-d: keep the shape)
-        t = torch.from_numpy(np.ascontiguousarray(a).reshape(a.shape)).to(self.device)
+        if a.ndim > 1 and not a.flags.c_contiguous:
+            # keep the array's axis order in memory (a later reduction sums
+            # in that order): upload the dense order-'K' copy, then permute
+            dense = np.array(a, order="K", copy=True)
+            order = _k_order([dense], dense.shape)
+            phys = np.ascontiguousarray(dense.transpose(order))
+            t = torch.from_numpy(phys).to(self.device).permute(_inverse(order))
+        else:
+            # (np.ascontiguousarray makes 0-d arrays 1-d: keep the shape)
+            t = torch.from_numpy(np.ascontiguousarray(a).reshape(a.shape)).to(self.device)
         try:
             self._consts[key] = (weakref.ref(v), t)
         except TypeError:
@@ -130,16 +146,27 @@ class BtRuntime:
 
     # ---- kernels ------------------------------------------------------------------
     def elementwise(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
+        out_shape = tuple(int(v) for v in out_shape)
+        back = None
+        if any(not t.is_contiguous() for t in inputs):
+            order = _k_order(inputs, out_shape)
+            if not _is_identity(order):
+                # numpy allocates the result in this axis order: run the
+                # kernel on the permuted views (contiguous output) and hand
+                # back the logical view
+                nd = len(out_shape)
+                inputs = [t.view((1,) * (nd - t.dim()) + tuple(t.shape)).permute(order) for t in inputs]
+                out_shape = tuple(out_shape[a] for a in order)
+                back = _inverse(order)
         out = self._empty(out_shape, out_dt)
-        if out.numel() == 0:
-            return out
-        descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
-        attrs = _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(compute_dt)], float(np.float32(alpha)))
-        od = tensor_desc(out)
-        self._stream()
-        check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
-        self.launches += 1
-        return out
+        if out.numel() > 0:
+            descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
+            attrs = _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(compute_dt)], float(np.float32(alpha)))
+            od = tensor_desc(out)
+            self._stream()
+            check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
+            self.launches += 1
+        return out if back is None else out.permute(back)
 
     # ---- data movement: strided copies through the IDENTITY kernel ----------------
     @staticmethod
@@ -218,7 +245,9 @@ class BtRuntime:
             offset += start * strides[a]
             strides[a] *= step
         dt = np_dtype(x)
-        out = self._empty(shape, dt)
+        # numpy's slice is a view in x's axis order: copy into that order
+        _, order = self._physical(x)
+        out = self._empty([shape[a] for a in order], dt).permute(_inverse(order))
         if out.numel() == 0:
             return out
         src = make_tensor(x.data_ptr() + offset * x.element_size(), dt, shape, strides)
@@ -236,11 +265,17 @@ class BtRuntime:
         return t
 
     def _contig(self, t):
-        if t.is_contiguous():
-            return t
-        dt = np_dtype(t)
-        cdt = np.float64 if dt.kind == "f" else np.int64
-        return self.elementwise("IDENTITY", [t], t.shape, dt, cdt)
+        """C-contiguous copy of a view (the copy kernel), t itself when it is one."""
+        return t if t.is_contiguous() else self._materialize(t)
+
+    def _physical(self, x):
+        """(phys, order): x's axes in its memory order (numpy's order 'K'),
+        phys = x.permute(order), a C-contiguous tensor when x is a dense
+        view; order is the identity for C-contiguous x."""
+        if x.is_contiguous():
+            return x, list(range(x.dim()))
+        order = _k_order([x], tuple(x.shape))
+        return x.permute(order), order
 
     # ---- the op table -----------------------------------------------------------------
     def dispatch(self, op, node_input, node_output, at, env):
@@ -369,8 +404,11 @@ class BtRuntime:
                 if name:
                     env[name] = p
             return
-        elif op == "Transpose":                                 # ref :517-518
-            out = self.transpose(dev(0), at.get("perm"))
+        elif op == "Transpose":                                 # ref :517-518 (view)
+            x = dev(0)
+            perm = at.get("perm")
+            nd = x.dim()
+            out = x.permute(list(range(nd))[::-1] if perm is None else [int(v) % max(nd, 1) for v in perm])
         elif op == "Concat":                                    # ref :531-535
             out = self.concat([self.to_device(env[i]) for i in node_input if i], at["axis"])
         elif op == "Slice":                                     # ref :548-549, :307-325
@@ -382,7 +420,11 @@ class BtRuntime:
             shape = [int(s) for s in _host_ints(arg(1))]
             if not at.get("allowzero", 0):
                 shape = [x.shape[i] if s == 0 else s for i, s in enumerate(shape)]
-            out = x.reshape(shape)
+            # a view where numpy's reshape gives one, else numpy's C-order copy
+            try:
+                out = x.view(shape)
+            except RuntimeError:
+                out = self._materialize(x).view(shape)
         elif op == "Unsqueeze":                                 # ref :519-523 (view)
             x = dev(0)
             axes = arg(1) if len(node_input) > 1 else at.get("axes")
@@ -513,6 +555,23 @@ class BtRuntime:
         dt = np_dtype(x)
         if dt != np.float32:
             raise NotImplementedError(f"{op} of {dt} is not on the GPU path (float32/float16 only)")
+        if not x.is_contiguous():
+            # numpy walks a view in its memory order: reduce the dense
+            # physical tensor over the same axes and view the result back
+            phys, order = self._physical(x)
+            if not _is_identity(order):
+                if not phys.is_contiguous():
+                    raise NotImplementedError(f"{op} of a permuted view with gaps is not on the GPU path")
+                r = self._reduce(op, phys, sorted(order.index(a) for a in norm), {"keepdims": 1})
+                r = r.permute(_inverse(order))
+                return r if keep else r.squeeze(tuple(norm))
+            # C order with gaps (a slice): numpy cannot merge the axes of a
+            # reduced block across a gap, so its pairwise runs would be shorter
+            for blk in _axis_blocks(norm, x.shape):
+                big = [a for a in blk if x.shape[a] != 1]
+                for a, b in zip(big, big[1:]):
+                    if x.stride(a) != x.stride(b) * x.shape[b]:
+                        raise NotImplementedError(f"{op} over axes {axes} of a strided view is not on the GPU path")
         x = self._contig(x)
         kind = 1 if op == "ReduceMean" else 0
         out_shape = [1 if i in norm else s for i, s in enumerate(x.shape)] if keep else \
@@ -557,6 +616,16 @@ class BtRuntime:
         return self.elementwise("DIV", [s, c], s.shape, np.float32, np.float64)
 
     def softmax(self, x, mask, axis):
+        if mask is None and not x.is_contiguous():
+            # numpy sums along the axis pairwise when it is innermost in
+            # memory: run the kernel on the physical order, view it back
+            nd = x.dim()
+            if axis < -nd or axis >= max(nd, 1):
+                raise np.exceptions.AxisError(axis, nd)
+            phys, order = self._physical(x)
+            if order[-1] != axis % nd:
+                raise NotImplementedError("Softmax along an axis that is not innermost in memory is not on the GPU path")
+            return self.softmax(self._contig(phys), None, -1).permute(_inverse(order))
         x = self._contig(x)
         out = self._empty(x.shape, np.float32)
         if out.numel() == 0:
@@ -571,6 +640,8 @@ class BtRuntime:
         return out
 
     def layernorm(self, x, skip, bias, gamma, beta, axis, eps):
+        if any(t is not None and not t.is_contiguous() for t in (x, skip, bias)):
+            return self._layernorm_view(x, skip, bias, gamma, beta, axis, eps)
         x = self._contig(self._as_f32(x))
         if skip is not None:
             skip = self._contig(self._as_f32(skip))
@@ -595,6 +666,49 @@ class BtRuntime:
                                     float(np.float32(eps)), tensor_desc(out)), "bt_layernorm")
         self.launches += 1
         return out
+
+    def _layernorm_view(self, x, skip, bias, gamma, beta, axis, eps):
+        """(Skip)LayerNormalization of views, in the order numpy walks them.
+        SkipLayerNormalization first forms s = x + skip (+ bias) as the
+        reference does (ref_runtime.py:604-609).  When the normalised axes
+        are innermost in memory, in order, the fused kernel runs on the
+        physical tensor (numpy's row sums are pairwise there too); otherwise
+        op_layernorm (ref_runtime.py:276-285) runs one numpy op at a time on
+        the physical order, where numpy's sums run slice after slice."""
+        f32 = np.float32
+        x = self._as_f32(x)
+        if skip is not None:
+            skip = self._as_f32(skip)
+            x = self.elementwise("ADD", [x, skip], np.broadcast_shapes(tuple(x.shape), tuple(skip.shape)), f32, f32)
+            if bias is not None:
+                bias = self._as_f32(bias)
+                x = self.elementwise("ADD", [x, bias], np.broadcast_shapes(tuple(x.shape), tuple(bias.shape)), f32, f32)
+        nd = x.dim()
+        ax = axis % nd
+        tail = list(range(ax, nd))
+        phys, order = self._physical(x)
+        if not phys.is_contiguous():
+            raise NotImplementedError("LayerNormalization of a strided view is not on the GPU path")
+        inv = _inverse(order)
+        if order[nd - len(tail):] == tail:
+            return self.layernorm(phys, None, None, gamma, beta, -len(tail), eps).permute(inv)
+        trailing = tuple(x.shape[ax:])
+        paxes = sorted(order.index(a) for a in tail)
+        mu = self._reduce("ReduceMean", phys, paxes, {"keepdims": 1})
+        d = self.elementwise("SUB", [phys, mu], phys.shape, f32, f32)
+        var = self._reduce("ReduceMean", self.elementwise("MUL", [d, d], d.shape, f32, f32), paxes, {"keepdims": 1})
+        e = torch.tensor(np.float32(eps)).to(self.device)
+        sd = self.elementwise("SQRT", [self.elementwise("ADD", [var, e], var.shape, f32, f32)], var.shape, f32, f32)
+        y = self.elementwise("DIV", [d, sd], d.shape, f32, f32)
+
+        def param(p):
+            p = self._contig(self._as_f32(self._fit_param(p, trailing)))
+            return p.view((1,) * ax + trailing).permute(order)
+
+        y = self.elementwise("MUL", [y, param(gamma)], y.shape, f32, f32)
+        if beta is not None:
+            y = self.elementwise("ADD", [y, param(beta)], y.shape, f32, f32)
+        return y.permute(inv)
 
     # ---- fused entry points (beyond the one-op-per-node table) ---------------------
     def chain(self, prog, inputs, out_shape):
@@ -701,6 +815,62 @@ def _host_ints(v):
     if isinstance(v, torch.Tensor):
         v = v.detach().cpu().numpy()
     return np.asarray(v).reshape(-1).tolist()
+
+
+def _layout(t):
+    """(shape, strides in bytes) of a torch tensor or numpy array."""
+    if isinstance(t, torch.Tensor):
+        return tuple(t.shape), tuple(st * t.element_size() for st in t.stride())
+    a = np.asarray(t)
+    return a.shape, a.strides
+
+
+def _k_order(operands, out_shape):
+    """The axis order numpy's iterator picks for order 'K' over these operands
+    broadcast to out_shape (nditer's best-axis-ordering pass): a stable
+    insertion sort of the axes by stride, smallest first, in which each
+    operand with nonzero strides on both axes of a pair votes and C order
+    wins conflicts; broadcast and size-1 axes have stride 0 and do not vote.
+    Returns logical axes, outermost first (C order is range(nd))."""
+    nd = len(out_shape)
+    st = []
+    for t in operands:
+        shape, strides = _layout(t)
+        pad = nd - len(shape)
+        st.append([0 if i < pad or shape[i - pad] == 1 or out_shape[i] == 1 else strides[i - pad]
+                   for i in range(nd)])
+    perm = list(range(nd))[::-1]          # iterator position 0 = innermost
+    for i0 in range(1, nd):
+        ax0, ipos = perm[i0], i0
+        for i1 in range(i0 - 1, -1, -1):
+            ax1 = perm[i1]
+            ambig, swap = True, False
+            for s_ in st:
+                if s_[ax0] != 0 and s_[ax1] != 0:
+                    if abs(s_[ax1]) <= abs(s_[ax0]):
+                        swap = False
+                    elif ambig:
+                        swap = True
+                    ambig = False
+            if not ambig:
+                if swap:
+                    ipos = i1
+                else:
+                    break
+        if ipos != i0:
+            perm.insert(ipos, perm.pop(i0))
+    return perm[::-1]
+
+
+def _inverse(perm):
+    inv = [0] * len(perm)
+    for i, p in enumerate(perm):
+        inv[p] = i
+    return inv
+
+
+def _is_identity(perm):
+    return all(i == p for i, p in enumerate(perm))
 
 
 def ctypes_stream(stream):
