@@ -304,6 +304,12 @@ def per_op(rt, torch, peak):
     entry("dynquant_8MB", lambda: rt.dynamic_quantize(Xq), xq.size * 5 + 5,
           onode("DynamicQuantizeLinear", {"x": xq}, ["x"]))
     del Xq
+    # the model's typical quantised activations (one-cluster path)
+    for nm, shape in (("dynquant_128KB", (1, 128, 256)), ("dynquant_512KB", (1, 256, 512))):
+        xs = (np.random.default_rng(1).standard_normal(shape) * 2).astype(np.float32)
+        Xs_ = dev(xs)
+        entry(nm, lambda Xs_=Xs_: rt.dynamic_quantize(Xs_), xs.size * 5 + 5,
+              onode("DynamicQuantizeLinear", {"x": xs}, ["x"]))
     # the integer convolution epilogue of a stage-0 conv output [1, 256, 4000]
     # (algorithmic bytes: int32 accumulators read, float32 written)
     gq = torch.Generator(device="cuda").manual_seed(0)
@@ -550,7 +556,7 @@ def run_profile_adain(args):
 
 
 PROFILE_OPS = ("reducemean_c2", "softmax_c3_b16", "layernorm_768", "reducemean_8192", "dynquant_256MB",
-               "conv_epilogue_256MB", "transpose_256MB", "tanh_256MB")
+               "conv_epilogue_256MB", "transpose_256MB", "tanh_256MB", "adain_dq_256MB")
 
 
 def run_profile_op(args):
@@ -559,7 +565,9 @@ def run_profile_op(args):
     (c3 masked softmax at batch 16) or 'layernorm_768' (LayerNormalization
     over 768 channels of a 256 MB tensor); the 256 MB sweep's
     'reducemean_8192', 'dynquant_256MB', 'conv_epilogue_256MB',
-    'transpose_256MB' ([64,128,8192] -> [64,8192,128]) and 'tanh_256MB'."""
+    'transpose_256MB' ([64,128,8192] -> [64,8192,128]), 'tanh_256MB' and
+    'adain_dq_256MB' (AdaIN+Snake with the range folded in, then the
+    quantize pass)."""
     import torch
     from bt_b200 import configs
     from bt_b200.runtime import BtRuntime
@@ -589,6 +597,15 @@ def run_profile_op(args):
             fn = lambda: rt.conv_int_epilogue(acc, b, xs, ws)
         elif name == "transpose_256MB":
             fn = lambda: rt.transpose(A, [0, 2, 1])
+        elif name == "adain_dq_256MB":
+            g = torch.rand((64, 128), device="cuda")
+            al = (torch.rand(128, device="cuda") + 0.5).half()
+            ial = (1.0 / al.float()).half()
+            rec, out = rt.range_records(1), [torch.empty_like(A)]
+
+            def fn():
+                rt.adain_snake([A], g, g, 1e-5, al, ial, outs=out, ranges=rec)
+                rt.dynamic_quantize(out[0], range=rec[0])
         else:
             fn = lambda: rt.elementwise("TANH", [A], A.shape, np.float32, np.float32)
     for _ in range(args.warmup + args.steps):

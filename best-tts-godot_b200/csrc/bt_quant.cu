@@ -18,7 +18,12 @@
 // the scale and zero-point outputs.  A NaN anywhere makes numpy's min and max
 // NaN, which Python's min(0.0, nan) and max(0.0, nan) turn into 0: scale 1,
 // zero point 0; the NaN elements themselves become 0 here (numpy's cast of
-// NaN to uint8 is platform-defined; 0 on x86-64).
+// NaN to uint8 is platform-defined; 0 on x86-64).  Aligned float32 inputs
+// of up to 2^17 values (most of the model's quantised activations) take one
+// launch of one thread-block cluster instead, which holds x in registers,
+// combines the range in distributed shared memory and needs neither the
+// scratch record nor its memset.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -33,6 +38,7 @@
 namespace bt {
 namespace {
 
+namespace cg = cooperative_groups;
 constexpr int kThreads = 256;
 
 // scratch[0] = ~ord(min) (atomicMax), scratch[1] = ord(max), scratch[2] = NaN seen
@@ -140,6 +146,110 @@ __global__ void __launch_bounds__(kThreads) dq_quantize_kernel(const T* x, int64
     y[i] = (uint8_t)q8(ldx(x, i), p);
 }
 
+// Small inputs: one launch of one cluster of kSmallCtas CTAs, x read once,
+// no scratch.  For float32 x on a 16-byte boundary of up to kSmallMax values
+// every thread loads its (at most kSmallVec) float4 groups into registers
+// at once, the CTA reduces them to a record in its shared memory (the
+// integer forms of the range record above), and after a cluster barrier
+// every CTA combines the kSmallCtas records through distributed shared
+// memory, derives scale and zero point as dq_quantize_kernel does and
+// quantizes the values it holds.  The second barrier keeps every CTA's
+// record alive until all have read it.
+constexpr int kSmallCtas = 8;
+constexpr int kSmallThreads = 512;
+constexpr int kSmallVec = 8;
+constexpr int64_t kSmallMax = (int64_t)kSmallCtas * kSmallThreads * kSmallVec * 4;   // 2^17 values
+
+__global__ void __cluster_dims__(kSmallCtas, 1, 1) __launch_bounds__(kSmallThreads, 1)
+    dq_cluster_kernel(const float* x, int64_t n, uint8_t* y, float* scale_out, uint8_t* zp_out) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  __shared__ uint32_t part[3];
+  __shared__ float slo[kSmallThreads / 32], shi[kSmallThreads / 32];
+  __shared__ int snan;
+  __shared__ DqParams sp;
+  const int t0 = rank * kSmallThreads + (int)threadIdx.x;
+  constexpr int stride = kSmallCtas * kSmallThreads;
+  const int nv = (int)(n >> 2);
+  const float4* xv = reinterpret_cast<const float4*>(x);
+  float4 v[kSmallVec];
+#pragma unroll
+  for (int k = 0; k < kSmallVec; ++k) {
+    const int q = t0 + k * stride;
+    if (q < nv) v[k] = __ldcs(xv + q);
+  }
+  // the n % 4 tail: threads 0..2 of CTA 0
+  const int tail = (rank == 0 && (int)threadIdx.x < (int)(n & 3)) ? (int)(nv << 2) + (int)threadIdx.x : -1;
+  const float tv = tail >= 0 ? x[tail] : 0.0f;
+  float lo = INFINITY, hi = -INFINITY;
+  bool nan = false;
+  auto take = [&](float f) {
+    nan |= f != f;
+    lo = fminf(lo, f);
+    hi = fmaxf(hi, f);
+  };
+#pragma unroll
+  for (int k = 0; k < kSmallVec; ++k)
+    if (t0 + k * stride < nv) {
+      take(v[k].x); take(v[k].y); take(v[k].z); take(v[k].w);
+    }
+  if (tail >= 0) take(tv);
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  nan = __any_sync(0xffffffffu, nan);
+  if (threadIdx.x == 0) snan = 0;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    slo[threadIdx.x >> 5] = lo;
+    shi[threadIdx.x >> 5] = hi;
+    if (nan) snan = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kSmallThreads / 32; ++w) {
+      lo = fminf(lo, slo[w]);
+      hi = fmaxf(hi, shi[w]);
+    }
+    part[0] = lo <= hi ? ~dq_ord(lo) : 0u;   // an all-NaN share keeps the identities
+    part[1] = lo <= hi ? dq_ord(hi) : 0u;
+    part[2] = snan ? 1u : 0u;
+  }
+  cluster.sync();
+  if (threadIdx.x < 32) {
+    // lane r reads CTA r's record; max / or across the lanes
+    uint32_t rec[3] = {0u, 0u, 0u};
+    if (threadIdx.x < kSmallCtas) {
+      const uint32_t* q = cluster.map_shared_rank(part, (int)threadIdx.x);
+      rec[0] = q[0];
+      rec[1] = q[1];
+      rec[2] = q[2];
+    }
+    for (int o = kSmallCtas / 2; o > 0; o >>= 1) {
+      rec[0] = max(rec[0], __shfl_xor_sync(0xffffffffu, rec[0], o));
+      rec[1] = max(rec[1], __shfl_xor_sync(0xffffffffu, rec[1], o));
+      rec[2] |= __shfl_xor_sync(0xffffffffu, rec[2], o);
+    }
+    if (threadIdx.x == 0) {
+      sp = dq_params(rec, n);
+      if (rank == 0) {
+        *scale_out = sp.scale32;
+        *zp_out = (uint8_t)sp.zp;
+      }
+    }
+  }
+  cluster.sync();
+  const DqParams p = sp;
+  uint32_t* yw = reinterpret_cast<uint32_t*>(y);
+#pragma unroll
+  for (int k = 0; k < kSmallVec; ++k) {
+    const int q = t0 + k * stride;
+    if (q < nv) __stcs(yw + q, q8(v[k].x, p) | (q8(v[k].y, p) << 8) | (q8(v[k].z, p) << 16) | (q8(v[k].w, p) << 24));
+  }
+  if (tail >= 0) y[tail] = (uint8_t)q8(tv, p);
+}
+
 // One 16-byte scratch record per (device, stream), allocated on first use.
 int scratch_for(int device, cudaStream_t s, uint32_t** out) {
   static std::mutex mu;
@@ -189,6 +299,12 @@ int dynamic_quantize_run(const bt_tensor* x, const bt_tensor* y, float* scale_ou
   int rc = dev_info(&di);
   if (rc) return rc;
   cudaStream_t s = cur_stream();
+  if (n <= kSmallMax && x->dtype == BT_F32 && ((uintptr_t)x->data & 15) == 0 && ((uintptr_t)y->data & 3) == 0) {
+    // one cluster, one launch, the scratch record unused
+    dq_cluster_kernel<<<kSmallCtas, kSmallThreads, 0, s>>>((const float*)x->data, n, (uint8_t*)y->data, scale_out,
+                                                           zp_out);
+    return check_launch("bt_dynamic_quantize");
+  }
   cudaError_t e = cudaMemsetAsync(scratch, 0, 12, s);
   if (e != cudaSuccess) return set_error(BT_ECUDA, "bt_dynamic_quantize: memset: %s", cudaGetErrorString(e));
   int64_t blocks = (n + kThreads * 16 - 1) / (kThreads * 16);

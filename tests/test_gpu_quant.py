@@ -1,5 +1,7 @@
 """DynamicQuantizeLinear on the GPU (bt_dynamic_quantize) against the oracle,
 bit for bit: the uint8 values, the float32 scale and the uint8 zero point.
+Sizes on both sides of 2^17 values, where the one-cluster path for small
+aligned float32 inputs hands over to the two-kernel path.
 
 Sizes past one CTA's share and past the 16-value vector groups, inputs at
 every 4-byte phase (the element-wise paths), float16 input, one-signed and
@@ -44,7 +46,8 @@ def _check(rt, x, phase=0, what=""):
     assert_same(y, wy, f"values {what}")
 
 
-@pytest.mark.parametrize("n", [1, 15, 16, 17, 4097, 1 << 20, 3_000_001])
+@pytest.mark.parametrize("n", [1, 3, 15, 16, 17, 4097, 32_768, 100_003, (1 << 17) - 1, 1 << 17, (1 << 17) + 1,
+                               1 << 20, 3_000_001])
 def test_sizes(gpu_runtime, n):
     rng = np.random.default_rng(n)
     _check(gpu_runtime, (rng.standard_normal(n) * 2.5).astype(np.float32), what=f"n={n}")
@@ -59,6 +62,7 @@ def test_unaligned(gpu_runtime, phase):
 def test_float16_and_shapes(gpu_runtime):
     rng = np.random.default_rng(3)
     _check(gpu_runtime, (rng.standard_normal((4, 512, 333)) * 4).astype(np.float16), what="fp16")
+    _check(gpu_runtime, (rng.standard_normal((1, 512, 33)) * 4).astype(np.float16), what="fp16 small")
     _check(gpu_runtime, rng.uniform(0.1, 9.0, (2, 256, 4000)).astype(np.float32), what="positive")
     _check(gpu_runtime, -rng.uniform(0.1, 9.0, (2, 256, 4000)).astype(np.float32), what="negative")
     _check(gpu_runtime, np.full((7, 9), 2.5, np.float32), what="constant")

@@ -42,7 +42,9 @@ def test_noalloc_equals_allocating_entry_point_on_two_calls(lib):
     check(lib.bt_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "bt_set_stream")
     rng = np.random.default_rng(2024)
     inputs = [(rng.standard_normal((3, 512, 1001)) * 3.0 + 1.0).astype(np.float32),   # mixed signs
-              rng.uniform(0.25, 0.75, (2, 777)).astype(np.float32)]                   # positive, a narrower range
+              rng.uniform(0.25, 0.75, (2, 300_001)).astype(np.float32)]               # positive, a narrower range
+    # (both above 2^17 values: smaller inputs take the one-cluster path, which
+    # needs no scratch record at all)
     for k, xh in enumerate(inputs):
         x = torch.from_numpy(xh).cuda()
         got = _quantize(lib, "bt_dynamic_quantize_noalloc", x)
