@@ -481,8 +481,8 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
         }
         uint32_t* rec = A.range[k];
         if (rlo <= rhi) {   // not an all-NaN (or empty) segment
-          atomicMax(&rec[0], ~dq_ord(rlo));
-          atomicMax(&rec[1], dq_ord(rhi));
+          dq_raise(&rec[0], ~dq_ord(rlo));
+          dq_raise(&rec[1], dq_ord(rhi));
         }
         if (sr_nan) atomicOr(&rec[2], 1u);
       }

@@ -47,6 +47,13 @@ __device__ __forceinline__ float dq_from_ord(uint32_t o) {
   return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
+// atomicMax into a range-record word, skipped when the word already holds
+// at least v: the words only grow, so the result is the same, and most of a
+// large grid's CTAs then issue no atomic on the two contended addresses.
+__device__ __forceinline__ void dq_raise(uint32_t* w, uint32_t v) {
+  if (v > *(volatile const uint32_t*)w) atomicMax(w, v);
+}
+
 __device__ __forceinline__ DqParams dq_params_from(double scale, double z) {
   DqParams p;
   p.scale32 = __double2float_rn(scale);

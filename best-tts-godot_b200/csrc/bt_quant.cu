@@ -104,8 +104,8 @@ __global__ void __launch_bounds__(kThreads) dq_range_kernel(const T* x, int64_t 
     }
     // an all-NaN share leaves lo = +inf, hi = -inf: the identities
     if (lo <= hi) {
-      atomicMax(&scratch[0], ~dq_ord(lo));
-      atomicMax(&scratch[1], dq_ord(hi));
+      dq_raise(&scratch[0], ~dq_ord(lo));
+      dq_raise(&scratch[1], dq_ord(hi));
     }
     if (snan) atomicOr(&scratch[2], 1u);
   }
