@@ -358,8 +358,16 @@ class BtRuntime:
             target = np.dtype(ONNX_TO_NUMPY[at["to"]])
             if target == np.float16:
                 target = np.dtype(np.float32)
-            src = _wide(np_dtype(x))
-            out = self.elementwise("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
+            if np_dtype(x) == target and self._physical(x)[0].is_contiguous():
+                # astype to the dtype x already has: numpy copies the same
+                # values in the same axis order, and graph values are never
+                # written after they are made, so x itself serves (half of
+                # the model's Casts are float32 -> float32 once fp16 targets
+                # are elided, one before every DynamicQuantizeLinear)
+                out = x
+            else:
+                src = _wide(np_dtype(x))
+                out = self.elementwise("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
         elif op == "DequantizeLinear":                          # ref :631-636
             q, scale, zp = dev(0), dev(1), dev(2)
             ins = [q, scale] + ([zp] if zp is not None else [])

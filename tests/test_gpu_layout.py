@@ -101,3 +101,24 @@ def test_fortran_ordered_upload(gpu_runtime):
     nodes = [("LayerNormalization", ["x", "g", "b"], ["y"], {"axis": -1, "epsilon": 1e-5}),
              ("ReduceMean", ["x", "ax"], ["m"], {"keepdims": 1})]
     _run(gpu_runtime, nodes, env, ["y", "m"])
+
+
+def test_same_dtype_cast_launches_nothing(gpu_runtime):
+    """Cast to the dtype the tensor has (float32 -> float32, and the fp16
+    target the reference computes in float32) hands back the tensor itself;
+    a view with gaps is copied densely, as numpy's astype does."""
+    rng = np.random.default_rng(6)
+    env = {"x": rng.standard_normal((4, 96, 33)).astype(F32), "st": np.array([0], I64),
+           "en": np.array([20], I64), "axs": np.array([2], I64)}
+    nodes = [("Transpose", ["x"], ["xt"], {"perm": [0, 2, 1]}),
+             ("Cast", ["xt"], ["c1"], {"to": 1}),
+             ("Cast", ["c1"], ["c2"], {"to": 10}),
+             ("DynamicQuantizeLinear", ["c2"], ["q", "qs", "qz"], {}),
+             ("Slice", ["xt", "st", "en", "axs"], ["sl"], {}),
+             ("Cast", ["sl"], ["c3"], {"to": 1})]
+    _run(gpu_runtime, nodes, env, ["c1", "c2", "q", "qs", "qz", "sl", "c3"])
+    got = dict(env)
+    gpu_runtime.run_nodes(nodes[:1], got)
+    before = gpu_runtime.launches
+    gpu_runtime.run_nodes(nodes[1:3], got)
+    assert gpu_runtime.launches == before and got["c2"] is got["xt"]
