@@ -28,6 +28,7 @@ numpy's broadcasting rule.  Errors numpy would raise (bad broadcast, bad
 dtype) surface as the same exceptions before any launch; a status from the
 library raises ``BtError`` (a RuntimeError).
 """
+import ctypes
 import weakref
 
 import numpy as np
@@ -48,6 +49,7 @@ TORCH_TO_NP = {
     torch.float32: np.float32, torch.float64: np.float64,
 }
 NP_TO_TORCH = {np.dtype(v): k for k, v in TORCH_TO_NP.items()}
+TORCH_TO_BT = {k: _lib.NP_TO_BT[np.dtype(v)] for k, v in TORCH_TO_NP.items()}
 for _name in ("uint16", "uint32", "uint64"):
     if hasattr(torch, _name):
         TORCH_TO_NP[getattr(torch, _name)] = getattr(np, _name)
@@ -85,9 +87,15 @@ def _probe(dt):
     return np.empty((0,), dtype=dt)
 
 
+_I64x8 = ctypes.c_int64 * 8
+
+
 def tensor_desc(t):
     """BtTensor view of a CUDA tensor (element strides, arbitrary layout)."""
-    return make_tensor(t.data_ptr(), np_dtype(t), tuple(t.shape), tuple(t.stride()))
+    shape = t.shape
+    if len(shape) > 8:
+        raise ValueError(f"rank {len(shape)} exceeds 8")
+    return _lib.BtTensor(t.data_ptr(), TORCH_TO_BT[t.dtype], len(shape), _I64x8(*shape), _I64x8(*t.stride()))
 
 
 class BtRuntime:
@@ -142,7 +150,7 @@ class BtRuntime:
         return torch.empty(tuple(int(s) for s in shape), dtype=NP_TO_TORCH[np.dtype(dt)], device=self.device)
 
     def _stream(self):
-        check(self.lib.bt_set_stream(ctypes_stream(torch.cuda.current_stream(self.device))), "bt_set_stream")
+        check(self.lib.bt_set_stream(torch.cuda.current_stream(self.device).cuda_stream), "bt_set_stream")
 
     # ---- kernels ------------------------------------------------------------------
     def elementwise(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
