@@ -889,10 +889,4 @@ def _is_identity(perm):
     return all(i == p for i, p in enumerate(perm))
 
 
-def ctypes_stream(stream):
-    return stream.cuda_stream
-
-
-import ctypes  # noqa: E402
-
 ctypes_i64 = ctypes.c_int64
