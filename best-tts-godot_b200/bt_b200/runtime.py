@@ -29,6 +29,7 @@ dtype) surface as the same exceptions before any launch; a status from the
 library raises ``BtError`` (a RuntimeError).
 """
 import ctypes
+import functools
 import weakref
 
 import numpy as np
@@ -85,6 +86,33 @@ def _wide(dt):
 
 def _probe(dt):
     return np.empty((0,), dtype=dt)
+
+
+@functools.lru_cache(maxsize=256)
+def _ew_attrs(compute_dt, alpha):
+    """The attribute block of a launch (shared: the library only reads it)."""
+    return _lib.BtEwAttrs(_lib.NP_TO_BT[compute_dt], float(np.float32(alpha)))
+
+
+@functools.lru_cache(maxsize=4096)
+def _binary_result(op, a, b):
+    """numpy's result dtype of the binary op on arrays of dtypes a, b."""
+    if op == "Div" and a.kind in "iu" and b.kind in "iu":
+        return np.floor_divide(_probe(a), _probe(b)).dtype   # ref :452-455
+    f = {"Add": np.add, "Sub": np.subtract, "Mul": np.multiply, "Div": np.true_divide, "Pow": np.power}[op]
+    return f(_probe(a), _probe(b)).dtype
+
+
+def _raw_stream(device_index):
+    """The current CUDA stream of a device as an integer handle."""
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
+try:   # torch's own fast accessor of the same handle, where this torch has it
+    _fast = torch._C._cuda_getCurrentRawStream
+    _raw_stream = lambda device_index: _fast(device_index)   # noqa: E731
+except AttributeError:
+    pass
 
 
 _I64x8 = ctypes.c_int64 * 8
@@ -150,7 +178,7 @@ class BtRuntime:
         return torch.empty(tuple(int(s) for s in shape), dtype=NP_TO_TORCH[np.dtype(dt)], device=self.device)
 
     def _stream(self):
-        check(self.lib.bt_set_stream(torch.cuda.current_stream(self.device).cuda_stream), "bt_set_stream")
+        check(self.lib.bt_set_stream(_raw_stream(self.device.index)), "bt_set_stream")
 
     # ---- kernels ------------------------------------------------------------------
     def elementwise(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
@@ -169,7 +197,7 @@ class BtRuntime:
         out = self._empty(out_shape, out_dt)
         if out.numel() > 0:
             descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
-            attrs = _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(compute_dt)], float(np.float32(alpha)))
+            attrs = _ew_attrs(np.dtype(compute_dt), float(alpha))
             od = tensor_desc(out)
             self._stream()
             check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
@@ -300,12 +328,7 @@ class BtRuntime:
             x, y = dev(0), dev(1)
             a, b = _wide(np_dtype(x)), _wide(np_dtype(y))
             shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
-            if op == "Div" and a.kind in "iu" and b.kind in "iu":
-                dt = np.floor_divide(_probe(a), _probe(b)).dtype   # ref :452-455
-            else:
-                f = {"Add": np.add, "Sub": np.subtract, "Mul": np.multiply, "Div": np.true_divide,
-                     "Pow": np.power}[op]
-                dt = f(_probe(a), _probe(b)).dtype
+            dt = _binary_result(op, a, b)
             if op == "Pow" and dt.kind != "f":
                 raise NotImplementedError("integer Pow is not on the GPU path")
             name = {"Add": "ADD", "Sub": "SUB", "Mul": "MUL", "Div": "DIV", "Pow": "POW"}[op]
