@@ -18,6 +18,8 @@ A tensor therefore crosses between host and device only where its consumer
 runs on the other side, once per direction.  ``stats`` counts the nodes on
 each side and the bytes moved.
 """
+import weakref
+
 import numpy as np
 import torch
 
@@ -36,16 +38,19 @@ class HybridRuntime:
         unknown = self.gpu_ops - set(BtRuntime.HOT_OPS)
         if unknown:
             raise ValueError(f"not on the GPU path: {sorted(unknown)}")
-        self._host = {}       # id(CUDA tensor) -> (tensor, its host copy)
+        self._host = {}       # id(CUDA tensor) -> (weak reference to it, its host copy)
         self.stats = {"gpu_nodes": 0, "cpu_nodes": 0, "d2h_bytes": 0}
 
     def _to_host(self, t):
         hit = self._host.get(id(t))
-        if hit is not None and hit[0] is t:
+        if hit is not None and hit[0]() is t:
             return hit[1]
         a = host_array(t, self._dense)
         self.stats["d2h_bytes"] += a.nbytes
-        self._host[id(t)] = (t, a)
+        if len(self._host) >= 1024:
+            # forget the copies of device tensors that no longer exist
+            self._host = {k: v for k, v in self._host.items() if v[0]() is not None}
+        self._host[id(t)] = (weakref.ref(t), a)
         return a
 
     def dispatch(self, op, node_input, node_output, at, env):

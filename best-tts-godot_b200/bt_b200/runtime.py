@@ -170,6 +170,9 @@ class BtRuntime:
             t = torch.from_numpy(np.ascontiguousarray(a).reshape(a.shape)).to(self.device)
         try:
             self._consts[key] = (weakref.ref(v), t)
+            # the device copy lives as long as the array: a long run that
+            # uploads many host results does not accumulate them
+            weakref.finalize(v, self._consts.pop, key, None)
         except TypeError:
             pass
         return t

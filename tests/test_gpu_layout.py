@@ -122,3 +122,16 @@ def test_same_dtype_cast_launches_nothing(gpu_runtime):
     before = gpu_runtime.launches
     gpu_runtime.run_nodes(nodes[1:3], got)
     assert gpu_runtime.launches == before and got["c2"] is got["xt"]
+
+
+def test_upload_cache_follows_the_host_array(gpu_runtime):
+    """An uploaded numpy array is reused while it lives and forgotten (its
+    device copy released) when it dies."""
+    import gc
+    a = np.arange(1024, dtype=F32)
+    t1 = gpu_runtime.to_device(a)
+    assert gpu_runtime.to_device(a) is t1
+    n = len(gpu_runtime._consts)
+    del a, t1
+    gc.collect()
+    assert len(gpu_runtime._consts) == n - 1

@@ -94,3 +94,15 @@ def test_host_array_keeps_axis_order():
     assert sorted(range(3), key=lambda i: -a.strides[i]) == [0, 2, 1]
     s = base[:, ::2, :].permute(0, 2, 1)           # a view with gaps: made dense first
     assert np.array_equal(host_array(s), s.numpy())
+
+
+def test_host_copies_do_not_keep_device_tensors_alive():
+    import gc
+    import weakref
+    hy = HybridRuntime(CountingCpu(), gpu_ops={"Add"}, gpu_runtime=TensorTable())
+    env = {"a": np.ones(8, np.float32), "b": np.ones(8, np.float32)}
+    hy.run_nodes([("Add", ["a", "b"], ["c"], {}), ("Sigmoid", ["c"], ["d"], {})], env)
+    ref = weakref.ref(env["c"])
+    del env["c"]
+    gc.collect()
+    assert ref() is None
