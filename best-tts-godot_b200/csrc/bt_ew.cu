@@ -591,41 +591,55 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
 // conflicts), so both the reads (along m) and the writes (along n) are
 // coalesced; a strided element-by-element copy would fetch a 32-byte sector
 // for every 4-byte read.  W is the element's byte width; bits are copied.
-template <typename W>
-__global__ void __launch_bounds__(256) transpose_kernel(const W* in, W* out, int64_t B, int64_t M, int64_t N,
-                                                        int64_t sb, int64_t sn) {
+// The grid walks batches (z), m tiles (y) and n tiles (x) by increments, so
+// no thread divides to find its tile.  VEC (4-byte elements, 16-byte aligned
+// rows and strides): each thread reads four consecutive m of one column as
+// one 128-bit load and writes four consecutive n of one row as one 128-bit
+// store; the tile's column (4q + j of row n) and row (4p + i, column m)
+// accesses both land on 32 distinct banks.
+template <typename W, bool VEC>
+__global__ void __launch_bounds__(256) transpose_kernel(const W* in, W* out, int64_t B, int M, int N, int64_t sb,
+                                                        int64_t sn) {
   __shared__ W tile[32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
-  // tile coordinates in 32-bit (the host sends M, N < 2^30)
-  const int tm = (int)((M + 31) >> 5), tn = (int)((N + 31) >> 5);
-  const int64_t per_b = (int64_t)tm * tn, tiles = B * per_b;
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int64_t b = t / per_b;
-    const int r = (int)(t - b * per_b);
-    const int m0 = (r / tn) << 5, n0 = (r % tn) << 5;
-    const W* src = in + b * sb + m0 + (int64_t)n0 * sn;   // element (m0, n0) of batch b
-    W* dst = out + b * M * N + (int64_t)m0 * N + n0;       // element (m0, n0) of the output
-    if (m0 + 32 <= M && n0 + 32 <= N) {
-      // a full tile: no bounds checks
-      const W* s0 = src + tx + ty * sn;
+  const int hi = threadIdx.x >> 3, lo = threadIdx.x & 7;    // 32 x 8 threads, 4 values each (VEC)
+  for (int64_t b = blockIdx.z; b < B; b += gridDim.z)
+    for (int m0 = blockIdx.y * 32; m0 < M; m0 += gridDim.y * 32)
+      for (int n0 = blockIdx.x * 32; n0 < N; n0 += gridDim.x * 32) {
+        const W* src = in + b * sb + m0 + (int64_t)n0 * sn;                 // element (m0, n0) of batch b
+        W* dst = out + b * (int64_t)M * N + (int64_t)m0 * N + n0;          // element (m0, n0) of the output
+        if (m0 + 32 <= M && n0 + 32 <= N) {
+          // a full tile: no bounds checks
+          if constexpr (VEC) {
+            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)hi * sn + 4 * lo));
+            tile[hi][4 * lo] = v.x;
+            tile[hi][4 * lo + 1] = v.y;
+            tile[hi][4 * lo + 2] = v.z;
+            tile[hi][4 * lo + 3] = v.w;
+            __syncthreads();
+            __stcs(reinterpret_cast<uint4*>(dst + (int64_t)hi * N + 4 * lo),
+                   make_uint4(tile[4 * lo][hi], tile[4 * lo + 1][hi], tile[4 * lo + 2][hi], tile[4 * lo + 3][hi]));
+          } else {
+            const W* s0 = src + tx + ty * sn;
 #pragma unroll
-      for (int k = 0; k < 32; k += 8) tile[ty + k][tx] = s0[k * sn];
-      __syncthreads();
-      W* d0 = dst + tx + (int64_t)ty * N;
+            for (int k = 0; k < 32; k += 8) tile[ty + k][tx] = s0[k * sn];
+            __syncthreads();
+            W* d0 = dst + tx + (int64_t)ty * N;
 #pragma unroll
-      for (int k = 0; k < 32; k += 8) d0[(int64_t)k * N] = tile[tx][ty + k];
-    } else {
-      const int mr = (int)(M - m0 < 32 ? M - m0 : 32), nr = (int)(N - n0 < 32 ? N - n0 : 32);
+            for (int k = 0; k < 32; k += 8) d0[(int64_t)k * N] = tile[tx][ty + k];
+          }
+        } else {
+          const int mr = M - m0 < 32 ? M - m0 : 32, nr = N - n0 < 32 ? N - n0 : 32;
 #pragma unroll
-      for (int k = ty; k < 32; k += 8)
-        if (tx < mr && k < nr) tile[k][tx] = src[tx + k * sn];
-      __syncthreads();
+          for (int k = ty; k < 32; k += 8)
+            if (tx < mr && k < nr) tile[k][tx] = src[tx + k * sn];
+          __syncthreads();
 #pragma unroll
-      for (int k = ty; k < 32; k += 8)
-        if (k < mr && tx < nr) dst[(int64_t)k * N + tx] = tile[tx][k];
-    }
-    __syncthreads();
-  }
+          for (int k = ty; k < 32; k += 8)
+            if (k < mr && tx < nr) dst[(int64_t)k * N + tx] = tile[tx][k];
+        }
+        __syncthreads();
+      }
 }
 
 // ---- launch helpers ---------------------------------------------------------------
@@ -739,13 +753,27 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
     const bool out_dense = p.st[1][r - 1] == 1 && p.st[1][r - 2] == N && (r == 2 || p.st[1][0] == M * N);
     const int64_t sn = p.st[0][r - 1], sb = r == 3 ? p.st[0][0] : 0;
     if (out_dense && p.st[0][r - 2] == 1 && sn != 1 && M >= 8 && N >= 8 && M < (1ll << 30) && N < (1ll << 30)) {
-      const int64_t tiles = B * ((M + 31) / 32) * ((N + 31) / 32);
-      const int g = (int)(tiles < 2147483647 ? tiles : 2147483647);
+      // grid: batches in z, m tiles in y, n tiles in x (each CTA walks the
+      // rest by increments), about 32 CTAs per SM in all
+      const int64_t tm = (M + 31) / 32, tn = (N + 31) / 32;
+      const int64_t gz = B < 65535 ? B : 65535, gy = tm < 65535 ? tm : 65535;
+      DevInfo di;
+      const int sms = (dev_info(&di) == BT_OK && di.sm_count > 0) ? di.sm_count : 148;
+      int64_t gx = ((int64_t)sms * 32 + gy * gz - 1) / (gy * gz);
+      if (gx > tn) gx = tn;
+      if (gx < 1) gx = 1;
+      const dim3 g((unsigned)gx, (unsigned)gy, (unsigned)gz);
+      const int Mi = (int)M, Ni = (int)N;
+      const bool vec = dtype_size(out->dtype) == 4 && ((uintptr_t)in[0].data & 15) == 0 &&
+                       ((uintptr_t)out->data & 15) == 0 && sn % 4 == 0 && sb % 4 == 0 && N % 4 == 0;
       switch (dtype_size(out->dtype)) {
-        case 1: transpose_kernel<uint8_t><<<g, 256, 0, s>>>((const uint8_t*)in[0].data, (uint8_t*)out->data, B, M, N, sb, sn); break;
-        case 2: transpose_kernel<uint16_t><<<g, 256, 0, s>>>((const uint16_t*)in[0].data, (uint16_t*)out->data, B, M, N, sb, sn); break;
-        case 4: transpose_kernel<uint32_t><<<g, 256, 0, s>>>((const uint32_t*)in[0].data, (uint32_t*)out->data, B, M, N, sb, sn); break;
-        default: transpose_kernel<uint64_t><<<g, 256, 0, s>>>((const uint64_t*)in[0].data, (uint64_t*)out->data, B, M, N, sb, sn); break;
+        case 1: transpose_kernel<uint8_t, false><<<g, 256, 0, s>>>((const uint8_t*)in[0].data, (uint8_t*)out->data, B, Mi, Ni, sb, sn); break;
+        case 2: transpose_kernel<uint16_t, false><<<g, 256, 0, s>>>((const uint16_t*)in[0].data, (uint16_t*)out->data, B, Mi, Ni, sb, sn); break;
+        case 4:
+          if (vec) transpose_kernel<uint32_t, true><<<g, 256, 0, s>>>((const uint32_t*)in[0].data, (uint32_t*)out->data, B, Mi, Ni, sb, sn);
+          else transpose_kernel<uint32_t, false><<<g, 256, 0, s>>>((const uint32_t*)in[0].data, (uint32_t*)out->data, B, Mi, Ni, sb, sn);
+          break;
+        default: transpose_kernel<uint64_t, false><<<g, 256, 0, s>>>((const uint64_t*)in[0].data, (uint64_t*)out->data, B, Mi, Ni, sb, sn); break;
       }
       return check_launch("bt_elementwise(transpose)");
     }

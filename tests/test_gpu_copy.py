@@ -82,3 +82,28 @@ def test_expand(gpu_runtime):
     got, want = _both(gpu_runtime, nodes, env)
     assert_same(got["y"], want["y"], "expand fp32")
     assert_same(got["z"], want["z"], "expand fp16")
+
+
+@pytest.mark.parametrize("shape,perm", [((2, 256, 4000), [0, 2, 1]), ((1, 510, 768), [0, 2, 1]), ((3, 33, 70), [0, 2, 1]),
+                                        ((64, 40), [1, 0]), ((5, 96, 128), [0, 2, 1]), ((12, 510, 64), [1, 0, 2]),
+                                        ((4, 37, 3, 5), [3, 1, 0, 2]), ((2, 8, 9), [0, 2, 1])])
+def test_transpose_kernel(gpu_runtime, shape, perm):
+    """The materialising transpose (BtRuntime.transpose: the tiled copy
+    kernel), every element width, full and edge tiles, the 128-bit path
+    (4-byte elements, aligned) and its scalar fallback (a start or a stride
+    off the 16-byte grid)."""
+    rng = np.random.default_rng(sum(shape))
+    for dt in (np.float32, np.int32, np.float16, np.int64, np.uint8):
+        x = (rng.standard_normal(shape) * 50).astype(dt)
+        xd = torch.from_numpy(x).cuda()
+        got = gpu_runtime.transpose(xd, perm)
+        assert got.is_contiguous()
+        assert_same(got.cpu().numpy(), np.ascontiguousarray(np.transpose(x, perm)), f"{shape} {perm} {dt}")
+    # start one element off a 16-byte boundary, and an odd row stride
+    x = rng.standard_normal(shape).astype(np.float32)
+    buf = torch.empty(x.size + 1, device="cuda")
+    off = buf[1:].view(shape)
+    off.copy_(torch.from_numpy(x))
+    assert_same(gpu_runtime.transpose(off, perm).cpu().numpy(), np.ascontiguousarray(np.transpose(x, perm)), "offset")
+    wide = torch.from_numpy(np.concatenate([x, x[..., :1]], axis=-1)).cuda()[..., : shape[-1]]
+    assert_same(gpu_runtime.transpose(wide, perm).cpu().numpy(), np.ascontiguousarray(np.transpose(x, perm)), "stride")
