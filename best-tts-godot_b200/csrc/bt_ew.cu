@@ -591,8 +591,9 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
 // conflicts), so both the reads (along m) and the writes (along n) are
 // coalesced; a strided element-by-element copy would fetch a 32-byte sector
 // for every 4-byte read.  W is the element's byte width; bits are copied.
-// The grid walks batches (z), m tiles (y) and n tiles (x) by increments, so
-// no thread divides to find its tile.  VEC (4-byte elements, 16-byte aligned
+// The grid walks batches (z), pairs of m tiles (y) and n tiles (x) by
+// increments, so no thread divides to find its tile; the two tiles of a pair
+// are read before either is written.  VEC (4-byte elements, 16-byte aligned
 // rows and strides): each thread reads four consecutive m of one column as
 // one 128-bit load and writes four consecutive n of one row as one 128-bit
 // store; the tile's column (4q + j of row n) and row (4p + i, column m)
@@ -600,43 +601,67 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
 template <typename W, bool VEC>
 __global__ void __launch_bounds__(256) transpose_kernel(const W* in, W* out, int64_t B, int M, int N, int64_t sb,
                                                         int64_t sn) {
-  __shared__ W tile[32][33];
+  __shared__ W tile[2][32][33];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 32 x 8 threads
   const int hi = threadIdx.x >> 3, lo = threadIdx.x & 7;    // 32 x 8 threads, 4 values each (VEC)
+  // one tile (m0, n0) through tile buffer u, any shape, bounds-checked
+  auto one_tile = [&](const W* src, W* dst, int mr, int nr, int u) {
+#pragma unroll
+    for (int k = ty; k < 32; k += 8)
+      if (tx < mr && k < nr) tile[u][k][tx] = src[tx + k * sn];
+    __syncthreads();
+#pragma unroll
+    for (int k = ty; k < 32; k += 8)
+      if (k < mr && tx < nr) dst[(int64_t)k * N + tx] = tile[u][tx][k];
+  };
   for (int64_t b = blockIdx.z; b < B; b += gridDim.z)
-    for (int m0 = blockIdx.y * 32; m0 < M; m0 += gridDim.y * 32)
+    for (int m0 = blockIdx.y * 64; m0 < M; m0 += gridDim.y * 64)
       for (int n0 = blockIdx.x * 32; n0 < N; n0 += gridDim.x * 32) {
         const W* src = in + b * sb + m0 + (int64_t)n0 * sn;                 // element (m0, n0) of batch b
         W* dst = out + b * (int64_t)M * N + (int64_t)m0 * N + n0;          // element (m0, n0) of the output
-        if (m0 + 32 <= M && n0 + 32 <= N) {
-          // a full tile: no bounds checks
-          if constexpr (VEC) {
-            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)hi * sn + 4 * lo));
-            tile[hi][4 * lo] = v.x;
-            tile[hi][4 * lo + 1] = v.y;
-            tile[hi][4 * lo + 2] = v.z;
-            tile[hi][4 * lo + 3] = v.w;
-            __syncthreads();
-            __stcs(reinterpret_cast<uint4*>(dst + (int64_t)hi * N + 4 * lo),
-                   make_uint4(tile[4 * lo][hi], tile[4 * lo + 1][hi], tile[4 * lo + 2][hi], tile[4 * lo + 3][hi]));
-          } else {
-            const W* s0 = src + tx + ty * sn;
-#pragma unroll
-            for (int k = 0; k < 32; k += 8) tile[ty + k][tx] = s0[k * sn];
-            __syncthreads();
-            W* d0 = dst + tx + (int64_t)ty * N;
-#pragma unroll
-            for (int k = 0; k < 32; k += 8) d0[(int64_t)k * N] = tile[tx][ty + k];
-          }
-        } else {
-          const int mr = M - m0 < 32 ? M - m0 : 32, nr = N - n0 < 32 ? N - n0 : 32;
-#pragma unroll
-          for (int k = ty; k < 32; k += 8)
-            if (tx < mr && k < nr) tile[k][tx] = src[tx + k * sn];
+        const int nr = N - n0 < 32 ? N - n0 : 32;
+        if (VEC && m0 + 64 <= M && nr == 32) {
+          // two full tiles, (m0, n0) and (m0 + 32, n0): both 128-bit loads
+          // in flight before either tile is stored
+          const uint4 v0 = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)hi * sn + 4 * lo));
+          const uint4 v1 = __ldcs(reinterpret_cast<const uint4*>(src + 32 + (int64_t)hi * sn + 4 * lo));
+          tile[0][hi][4 * lo] = v0.x;
+          tile[0][hi][4 * lo + 1] = v0.y;
+          tile[0][hi][4 * lo + 2] = v0.z;
+          tile[0][hi][4 * lo + 3] = v0.w;
+          tile[1][hi][4 * lo] = v1.x;
+          tile[1][hi][4 * lo + 1] = v1.y;
+          tile[1][hi][4 * lo + 2] = v1.z;
+          tile[1][hi][4 * lo + 3] = v1.w;
           __syncthreads();
 #pragma unroll
-          for (int k = ty; k < 32; k += 8)
-            if (k < mr && tx < nr) dst[(int64_t)k * N + tx] = tile[tx][k];
+          for (int u = 0; u < 2; ++u)
+            __stcs(reinterpret_cast<uint4*>(dst + (int64_t)(32 * u + hi) * N + 4 * lo),
+                   make_uint4(tile[u][4 * lo][hi], tile[u][4 * lo + 1][hi], tile[u][4 * lo + 2][hi],
+                              tile[u][4 * lo + 3][hi]));
+        } else if (!VEC && m0 + 64 <= M && nr == 32) {
+          // two full tiles, no bounds checks
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const W* s0 = src + 32 * u + tx + ty * sn;
+#pragma unroll
+            for (int k = 0; k < 32; k += 8) tile[u][ty + k][tx] = s0[k * sn];
+          }
+          __syncthreads();
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            W* d0 = dst + (int64_t)32 * u * N + tx + (int64_t)ty * N;
+#pragma unroll
+            for (int k = 0; k < 32; k += 8) d0[(int64_t)k * N] = tile[u][tx][ty + k];
+          }
+        } else {
+          // the edges: each of the (at most) two tiles on its own
+          const int mr0 = M - m0 < 32 ? M - m0 : 32;
+          one_tile(src, dst, mr0, nr, 0);
+          if (m0 + 32 < M) {
+            const int mr1 = M - m0 - 32 < 32 ? M - m0 - 32 : 32;
+            one_tile(src + 32, dst + (int64_t)32 * N, mr1, nr, 1);
+          }
         }
         __syncthreads();
       }
@@ -755,7 +780,7 @@ extern "C" int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_te
     if (out_dense && p.st[0][r - 2] == 1 && sn != 1 && M >= 8 && N >= 8 && M < (1ll << 30) && N < (1ll << 30)) {
       // grid: batches in z, m tiles in y, n tiles in x (each CTA walks the
       // rest by increments), about 32 CTAs per SM in all
-      const int64_t tm = (M + 31) / 32, tn = (N + 31) / 32;
+      const int64_t tm = (M + 63) / 64, tn = (N + 31) / 32;   // tm: pairs of m tiles
       const int64_t gz = B < 65535 ? B : 65535, gy = tm < 65535 ? tm : 65535;
       DevInfo di;
       const int sms = (dev_info(&di) == BT_OK && di.sm_count > 0) ? di.sm_count : 148;
