@@ -800,6 +800,50 @@ __global__ void __launch_bounds__(256) wrow_reduce_kernel(WReduceArgs A) {
   }
 }
 
+// Rows of NL x 128 float32 (1024 or 2048 values), whose pairwise tree is
+// perfect with 128-value leaves, summed straight from global memory: lane
+// j of group g (four lanes per leaf) holds numpy's accumulators r[2j],
+// r[2j+1] of leaves g and g + 8 as float2 and adds step m of each (one
+// 8-byte load per leaf and step: a warp load covers eight leaves, 32 bytes
+// each), the same additions in the same order as warp_pw_sum's float2 path.
+// No shared memory, so occupancy is not bound by staging whole rows.
+template <int NL>
+__global__ void __launch_bounds__(256) wrow_reduce_direct_kernel(const float* x, int mean, int64_t rows, float* out) {
+  constexpr int LPG = NL / 8;   // leaves per lane group
+  const int lane = threadIdx.x & 31, g = lane >> 2, j = lane & 3;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    const float2* r = reinterpret_cast<const float2*>(x + row * (int64_t)(NL * 128));
+    float2 acc[LPG];
+#pragma unroll
+    for (int t = 0; t < LPG; ++t) acc[t] = pk(-0.0f);   // -0.0 + x == x: acc starts as numpy's r[j] = a[j]
+#pragma unroll
+    for (int m = 0; m < 16; ++m)
+#pragma unroll
+      for (int t = 0; t < LPG; ++t) acc[t] = pk_add(acc[t], __ldcs(r + (g + 8 * t) * 64 + 4 * m + j));
+    // numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) per leaf
+    float ls[LPG];
+#pragma unroll
+    for (int t = 0; t < LPG; ++t) {
+      float v = BT_ADD(acc[t].x, acc[t].y);
+      v = BT_ADD(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      v = BT_ADD(v, __shfl_xor_sync(0xffffffffu, v, 2));
+      ls[t] = v;
+    }
+    // leaf L's sum into lane L, then the perfect tree by xor shuffles (as
+    // warp_heap_total sums a perfect tree)
+    const float v0 = __shfl_sync(0xffffffffu, ls[0], 4 * (lane & 7));
+    const float v1 = __shfl_sync(0xffffffffu, ls[LPG - 1], 4 * (lane & 7));
+    float total = lane < 8 ? v0 : (lane < NL ? v1 : 0.0f);
+#pragma unroll
+    for (int m = 1; m < NL; m <<= 1) total = BT_ADD(total, __shfl_xor_sync(0xffffffffu, total, m));
+    if (lane == 0) {
+      const float sum = BT_ADD(0.0f, total);
+      out[row] = mean ? np_mean_from_sum(sum, NL * 128) : sum;
+    }
+  }
+}
+
 // Writes o[i] = f(b[i]) for the row, 128-bit where o shares g's phase.
 template <class F>
 __device__ __forceinline__ void warp_write(float* o, const float* b, const float* g, int n, F f) {
@@ -1374,6 +1418,17 @@ extern "C" int bt_reduce(int kind, const bt_tensor* x, const int64_t* axes, int 
       size_t smem;
       int grid;
       rc = wrow_setup((int)R, O, &smem, &grid);
+      if (rc == BT_OK && x->dtype == BT_F32 && wp.perfect && (wp.n_leaf == 8 || wp.n_leaf == 16) &&
+          (int64_t)wp.n_leaf * 128 == R && ((uintptr_t)x->data & 7) == 0) {
+        // perfect trees of 128-value leaves: straight from global memory
+        if (wp.n_leaf == 8)
+          wrow_reduce_direct_kernel<8><<<grid, 32 * kWarpsPerCta, 0, s>>>((const float*)x->data, kind == BT_REDUCE_MEAN,
+                                                                         O, (float*)out->data);
+        else
+          wrow_reduce_direct_kernel<16><<<grid, 32 * kWarpsPerCta, 0, s>>>((const float*)x->data, kind == BT_REDUCE_MEAN,
+                                                                          O, (float*)out->data);
+        return check_launch("bt_reduce(warp rows, direct)");
+      }
       if (rc == BT_OK) {
         WReduceArgs a{wp, x->data, x->dtype, kind == BT_REDUCE_MEAN, O, (float*)out->data};
         wrow_reduce_kernel<<<grid, 32 * kWarpsPerCta, smem, s>>>(a);

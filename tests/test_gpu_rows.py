@@ -86,3 +86,26 @@ def test_warp_rows_layernorm(gpu_runtime, n):
     assert_same(got["z"], want["z"], f"skip layernorm n={n}")
     assert_same(got["y32"], want["y32"], f"layernorm fp32 gamma/beta n={n}")
     assert_same(got["y32n"], want["y32n"], f"layernorm fp32 gamma, no beta n={n}")
+
+
+@pytest.mark.parametrize("n", [1024, 2048])
+def test_perfect_rows_direct_and_fallback(gpu_runtime, n):
+    """Rows of 1024 / 2048 values (perfect trees of 128-value leaves) summed
+    straight from global memory, on a [B, C, T] tensor like BASELINE's c2;
+    a base one element off an 8-byte boundary takes the staged kernel. Both
+    equal numpy bit for bit."""
+    import torch
+    rng = np.random.default_rng(n + 1)
+    x = (rng.standard_normal((4, 700, n)) * 2 + 0.3).astype(np.float32)
+    env = {"x": x, "ax": np.array([2], np.int64)}
+    nodes = [("ReduceMean", ["x", "ax"], ["m"], {"keepdims": 1}), ("ReduceSum", ["x", "ax"], ["s"], {"keepdims": 0})]
+    got, want = _run_both(gpu_runtime, nodes, env)
+    for k in ("m", "s"):
+        assert_same(got[k], want[k], f"{k} n={n}")
+    buf = torch.empty(x.size + 1, device="cuda")
+    xo = buf[1:].view(x.shape)
+    xo.copy_(torch.from_numpy(x))
+    got2 = {"x": xo, "ax": env["ax"]}
+    gpu_runtime.run_nodes(nodes, got2)
+    for k in ("m", "s"):
+        assert_same(got2[k], want[k], f"{k} n={n} offset")
