@@ -38,7 +38,7 @@ def test_warp_rows_reduce(gpu_runtime, n):
         assert_same(got[k], want[k], f"{k} n={n}")
 
 
-@pytest.mark.parametrize("n", [3001, 8192, 24001, 49152])
+@pytest.mark.parametrize("n", [3001, 4096, 8192, 24001, 49152])
 def test_long_rows_reduce(gpu_runtime, n):
     """Rows longer than the warp-staged kernels take, read straight from
     global memory by the warp-per-row sum (odd lengths: unaligned rows)."""
