@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(256, OP == BT_OP_TANH ? 1 : 0) ew_flat_op_kern
   // U vectors per thread per iteration, all loads issued before the math.
   // (one vector at a time where a call to an out-of-line path would
   // otherwise need a stack frame)
-  constexpr int U = (OP == BT_OP_DIV || OP == BT_OP_SIGMOID) ? 1 : 2;
+  constexpr int U = OP == BT_OP_DIV ? 1 : 2;
   for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
     float x[U][3][VEC];
 #pragma unroll
