@@ -400,10 +400,11 @@ __global__ void __launch_bounds__(256, OP == BT_OP_TANH ? 1 : 0) ew_flat_op_kern
   constexpr bool kTrig = !(VEC == 4 && OP < 0);   // see apply_f32
   const int64_t nv = a.n / VEC;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  // U vectors per thread per iteration, all loads issued before the math.
-  // (one vector at a time where a call to an out-of-line path would
-  // otherwise need a stack frame)
-  constexpr int U = OP == BT_OP_DIV ? 1 : 2;
+  // U vectors per thread per iteration, all loads issued before the math:
+  // four for sin, cos and LeakyRelu, two for the rest (measured per op on
+  // the 256 MB sweep), one for Div, where a call to an out-of-line path
+  // would otherwise need a stack frame.
+  constexpr int U = OP == BT_OP_DIV ? 1 : (OP == BT_OP_SIN || OP == BT_OP_COS || OP == BT_OP_LEAKYRELU) ? 4 : 2;
   for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
     float x[U][3][VEC];
 #pragma unroll
