@@ -376,6 +376,9 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 256;
 constexpr size_t kRangeRecordBytes = 16;
 static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(uint32_t)];
+// A call needs one range record whatever the size of x, so no request can
+// exceed the array: the limit is a build-time fact, not a run-time check.
+static_assert(kRangeRecordBytes <= kNoAllocScratchBytes, "the range record must fit the static scratch array");
 
 // The device address of g_noalloc_scratch on the current device, looked up
 // with cudaGetSymbolAddress by the first call on each device (in host code the
@@ -403,9 +406,6 @@ extern "C" int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* 
                                            uint8_t* zp_out) {
   int rc = dynamic_quantize_check(x, y, scale_out, zp_out, "bt_dynamic_quantize_noalloc");
   if (rc) return rc;
-  if (kRangeRecordBytes > kNoAllocScratchBytes)
-    return set_error(BT_ETOOBIG, "bt_dynamic_quantize_noalloc: needs %zu bytes of scratch, the static array holds %zu",
-                     kRangeRecordBytes, kNoAllocScratchBytes);
   DevInfo di;
   if ((rc = dev_info(&di))) return rc;
   uint32_t* scratch = nullptr;

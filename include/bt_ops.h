@@ -24,6 +24,10 @@
  *     calling thread's current CUDA device.
  *   - Entry points marked "host only" touch no GPU and may be called on a
  *     machine without one.
+ *   - Device addresses the library caches per device (the scratch records of
+ *     bt_dynamic_quantize and bt_dynamic_quantize_noalloc) belong to the
+ *     device's primary context: the library must not be used across a
+ *     cudaDeviceReset of a device it has run on.
  */
 #ifndef BT_OPS_H
 #define BT_OPS_H
@@ -253,11 +257,11 @@ int bt_dynamic_quantize(const bt_tensor* x, const bt_tensor* y, float* scale_out
  * its own pool, a serving process with a fixed memory budget, a real-time
  * loop where an allocation could stall or fail mid-frame): it allocates
  * nothing.  Its 16-byte range record lives in a 256-byte static device array
- * that every device loading the library keeps until exit; a request needing
- * more scratch than that is rejected (BT_ETOOBIG), and none does today.  The
- * first call on a device looks up the array's device address: make it before
- * any stream capture.  All calls on a device share the record, so calls that
- * overlap on the GPU race.
+ * that every device loading the library keeps until exit; a call needs that
+ * one record whatever the size of x, so no input is too large for it (the
+ * library checks this when it is built).  The first call on a device looks
+ * up the array's device address: make it before any stream capture.  All
+ * calls on a device share the record, so calls that overlap on the GPU race.
  * No counterpart in the reference: the reference's executor always allocates
  * its min/max scratch (executor.gd:1201-1206). */
 int bt_dynamic_quantize_noalloc(const bt_tensor* x, const bt_tensor* y,

@@ -108,7 +108,9 @@ def topology(kpk_runtime):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("BT_REFERENCE_CHECKOUT"),
+                    required="BT_REFERENCE_CHECKOUT" not in os.environ,
+                    help="path of a best-tts-godot checkout (or set BT_REFERENCE_CHECKOUT)")
     args = ap.parse_args()
     ref_runtime, kpk_runtime = import_reference(args.reference)
     rt = reference_runtime(ref_runtime)

@@ -52,7 +52,9 @@ def spec(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("BT_REFERENCE_CHECKOUT"),
+                    required="BT_REFERENCE_CHECKOUT" not in os.environ,
+                    help="path of a best-tts-godot checkout (or set BT_REFERENCE_CHECKOUT)")
     args = ap.parse_args()
     ref_runtime, kpk_runtime = G.import_reference(args.reference)
     import voice_util

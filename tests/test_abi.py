@@ -181,7 +181,7 @@ def test_fused_chain_validates_then_reports_withdrawn(lib):
 
 @pytest.mark.gpu
 def test_ctypes_binding_without_torch_tensors():
-    """The INTEGRATION.md recipe: device memory from the CUDA runtime through
+    """A caller without torch: device memory from the CUDA runtime through
     ctypes, one broadcast Add through bt_elementwise, numpy's bits back."""
     import ctypes
     import os
