@@ -3,23 +3,28 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 Headline workload: the ISTFTNet generator's elementwise /
-broadcast / reduction op stream for a batch of utterances (64 per GPU by
-default), features [512, 400] -> stages [256, 4000] and [128, 24001], conv
-and fc outputs as seeded stand-ins resident in HBM.  One step = the whole
-stream for the batch (49 kernel launches).  With torchrun (N > 1) every rank
-runs its own 64 utterances (utterance sharding, no collective on the data
-path; "scaling": "weak"), timing is the max over ranks.
+broadcast / reduction op stream for ONE fixed batch of 64 utterances,
+features [512, 400] -> stages [256, 4000] and [128, 24001], conv and fc
+outputs as seeded stand-ins resident in HBM.  One step = the whole stream for
+the batch (49 kernel launches per GPU).  With torchrun (N > 1) the batch is
+split by utterance (64 / N per rank, shard.split_utterances; "scaling":
+"strong"), every rank runs its share through its own FusedDecoder with no
+collective on the data path, and the job's time is the max over ranks.  At
+N > 1 the weak-scaling figure (64 utterances on every rank) is reported
+beside it under "weak".
 
-Printed (rank 0, one JSON line): utt/s over all ranks from CUDA events with
-inputs resident; ``e2e`` through FusedDecoder.run_host with pinned host
-buffers (features + fc outputs in, final stage output out, every step);
-``roofline`` for the dominant kernel (bt_adain_snake) from per-launch CUDA
-events; ``cpu_baseline`` = the numpy oracle on the host cores; ``per_op`` =
-each BASELINE op config c1-c4 (GB/s, fraction of the measured HBM peak and
-of the nominal 8 TB/s) plus a >= 256 MB sweep, each next to the oracle's
-single-core numpy time; ``clocks`` sampled with nvidia-smi during the timed
-region.  ``--impl reference`` times the oracle port (the reference's numpy
-op table, restated in oracle/) on the host cores instead.
+Printed (rank 0, one JSON line): utt/s of the whole batch from CUDA events
+with inputs resident; ``e2e`` through FusedDecoder.host_pipeline with pinned
+host buffers (features + fc outputs in, final stage output out, every step)
+and ``e2e_limit``, which names what bounds it (the device step or the
+device-to-host copy of the result); ``roofline`` for the dominant kernel
+(bt_adain_snake) from per-launch CUDA events; ``cpu_baseline`` = the numpy
+oracle on the host cores; ``per_op`` = each BASELINE op config c1-c4 (GB/s,
+fraction of the measured HBM peak and of the nominal 8 TB/s) plus a >= 256 MB
+sweep, each next to the oracle's single-core numpy time; ``clocks`` sampled
+with nvidia-smi during the timed region.  ``--impl reference`` times the
+oracle port (the reference's numpy op table, restated in oracle/) on the
+host cores instead.
 """
 import argparse
 import json
@@ -50,14 +55,24 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def rank_batches(total, n):
+    """Utterances of each rank when one batch of `total` is split over n GPUs."""
+    from bt_b200 import shard
+    return [shard.split_utterances(total, n, r)[1] for r in range(n)]
+
+
 def config(args, n):
     from bt_b200.decoder import stage_shapes
+    per = rank_batches(args.batch, n)
+    gpu_bytes = max(per) * 128 * (args.t0 * 60 + 1) * 4
     return {"workload": "c5: batched Kokoro-82M ISTFTNet decoder-stage op stream (BASELINE configs[4])",
-            "batch_per_gpu": args.batch, "global_batch": args.batch * n, "t0": args.t0,
+            "global_batch": args.batch, "batch_per_gpu": max(per), "batch_split": per, "t0": args.t0,
             "stage_shapes": [[c, t] for (_, _, c, t) in stage_shapes(args.t0)],
-            "parallelism": f"utterance-sharded over {n} GPU(s), no collective on the data path",
-            "l2": "no flush needed: inputs larger than L2 (each stage-2 tensor is "
-                  f"{args.batch * 128 * (args.t0 * 60 + 1) * 4 / 1e6:.0f} MB)",
+            "parallelism": f"dp{n}: one batch of {args.batch} utterances split by utterance over {n} GPU(s) "
+                           "(strong scaling), no collective on the data path",
+            "l2": "no flush needed: every step moves "
+                  f"{75.6 * max(per) / 64:.1f} GB per GPU through HBM, far more than L2, so no step starts "
+                  f"with the previous step's data cached (a stage-2 tensor is {gpu_bytes / 1e6:.0f} MB per GPU)",
             "launches_per_step": 49}
 
 
@@ -120,7 +135,7 @@ def run_reference(args):
               f"oracle/ops.py, the reference's op table restated), {args.steps} steps")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": n,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": DATA,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": DATA,
             "config": config(args, n),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -455,11 +470,77 @@ def model_hot_nodes(rt, torch):
             "note": "host clock around BtRuntime.dispatch of every node (Python dispatch included), inputs resident"}
 
 
+class RankStream:
+    """One rank's share of the job: its FusedDecoder over `batch` utterances,
+    conv stand-ins drawn on the device, pinned host buffers holding the
+    per-step inputs (features, fc outputs), all seeded per rank."""
+
+    def __init__(self, batch, t0, rank, dev):
+        from bt_b200.decoder import FusedDecoder, build_stream, fill_conv_standins, host_inputs
+        from bt_b200 import shard
+        import torch
+        self.batch = batch
+        self.S = build_stream(batch, t0=t0)
+        self.dec = FusedDecoder(self.S, dev)
+        fill_conv_standins(self.dec, seed=shard.rank_seed(17, rank))
+        host = host_inputs(self.S, seed=shard.rank_seed(100, rank))
+        self.hin, self.hout = self.dec.host_buffers()
+        self.dec.fill_host(self.hin, host)
+        self.dec.run_host(self.hin, self.hout)             # inputs resident from here on
+        torch.cuda.synchronize()
+
+    def device_steps(self, steps, warmup, barrier, record=None):
+        """Seconds for `steps` launches of the stream (CUDA events on the
+        launch stream, barrier + synchronize on both sides); returns
+        (seconds, kernel launches)."""
+        import torch
+        for _ in range(warmup):
+            self.dec.launch()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        launches = 0
+        for _ in range(steps):
+            launches += self.dec.launch(record=record)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / 1e3, launches
+
+    def e2e_steps(self, steps, warmup, barrier):
+        """Seconds for `steps` end-to-end steps through the host-buffer API
+        (FusedDecoder.host_pipeline: each step copies its inputs in from
+        pinned host memory and its result out, overlapped with the
+        neighbouring steps' compute); returns (seconds, h2d, d2h bytes per
+        step)."""
+        import torch
+        pipe = self.dec.host_pipeline(self.hin, self.hout)
+        for _ in range(warmup):
+            pipe.step()
+        pipe.finish()
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        h2d = d2h = 0
+        for _ in range(steps):
+            h2d, d2h = pipe.step()
+        pipe.finish()
+        f1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return f0.elapsed_time(f1) / 1e3, h2d, d2h
+
+    def release(self):
+        import torch
+        del self.dec, self.hin, self.hout
+        torch.cuda.empty_cache()
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
-    from bt_b200.decoder import (FusedDecoder, build_stream, fill_conv_standins, host_inputs,
-                                 stream_algorithmic_bytes, stream_launches)
+    from bt_b200.decoder import stream_algorithmic_bytes
     from bt_b200.runtime import BtRuntime
     from bt_b200 import shard
 
@@ -483,16 +564,10 @@ def run_b200(args):
         procs = max(1, min(cpu_cores(), args.cpu_procs))
         pool = cpu_pool(procs)
 
-    S = build_stream(args.batch, t0=args.t0)
-    dec = FusedDecoder(S, dev)
-    # rank r owns utterances shard.utterance_range(batch, r) of the job; its
-    # synthetic inputs are seeded per rank
-    fill_conv_standins(dec, seed=shard.rank_seed(17, rank))
-    host = host_inputs(S, seed=shard.rank_seed(100, rank))
-    hin, hout = dec.host_buffers()
-    dec.fill_host(hin, host)
-    dec.run_host(hin, hout)             # inputs resident from here on
-    torch.cuda.synchronize()
+    # this rank's share of the one batch (strong scaling): utterances
+    # shard.split_utterances(batch, n, rank), inputs seeded per rank
+    _, mine = shard.split_utterances(args.batch, n, rank)
+    rs = RankStream(mine, args.t0, rank, dev)
 
     def barrier():
         shard.barrier(dev)
@@ -500,25 +575,14 @@ def run_b200(args):
     def max_over_ranks(v):
         return shard.max_over_ranks(v, device=dev)
 
-    for _ in range(args.warmup):
-        dec.launch()
-    barrier()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
     record = []
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e0.record()
-    launches = 0
-    for _ in range(args.steps):
-        launches += dec.launch(record=record)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
+    dt, launches = rs.device_steps(args.steps, args.warmup, barrier, record=record)
     clk = clocks.stop()
-    elapsed = max_over_ranks(e0.elapsed_time(e1) / 1e3)
-    value = n * args.batch * args.steps / elapsed
+    elapsed = max_over_ranks(dt)
+    value = args.batch * args.steps / elapsed
     ms_step = 1e3 * elapsed / args.steps
 
     # dominant kernel: bt_adain_snake launches of the timed region
@@ -541,34 +605,48 @@ def run_b200(args):
                 "algorithmic_bytes_per_launch": round(ad_bytes / max(ad_n, 1)),
                 "avg_launch_ms": round(1e3 * ad_time / max(ad_n, 1), 4),
                 "share_of_step_time": round(ad_time / max(sum(kind_time.values()), 1e-12), 4)}
-    stream_bytes = stream_algorithmic_bytes(S)
+    stream_bytes = stream_algorithmic_bytes(rs.S)
+    stream_bytes_all = int(shard.sum_over_ranks(stream_bytes, device=dev))
 
-    # end to end through the host-buffer API: every step copies its inputs in
-    # from pinned host memory and its result out; the copies of one step
-    # overlap the neighbouring steps' compute (HostPipeline)
-    pipe = dec.host_pipeline(hin, hout)
-    for _ in range(args.warmup):
-        pipe.step()
-    pipe.finish()
-    torch.cuda.synchronize()
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record()
-    h2d = d2h = 0
-    for _ in range(args.steps):
-        h2d, d2h = pipe.step()
-    pipe.finish()
-    f1.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_s = max_over_ranks(f0.elapsed_time(f1) / 1e3)
-    e2e = {"value": n * args.batch * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "ms_per_step": round(1e3 * e2e_s / args.steps, 3),
-           "api": "FusedDecoder.host_pipeline(...).step() (pinned host buffers; each step's copies "
+    # end to end through the host-buffer API
+    e2e_dt, h2d, d2h = rs.e2e_steps(args.steps, args.warmup, barrier)
+    e2e_s = max_over_ranks(e2e_dt)
+    h2d_all = int(shard.sum_over_ranks(h2d, device=dev))
+    d2h_all = int(shard.sum_over_ranks(d2h, device=dev))
+    e2e = {"value": args.batch * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d_all,
+           "d2h_bytes_per_step": d2h_all, "ms_per_step": round(1e3 * e2e_s / args.steps, 3),
+           "api": "FusedDecoder.host_pipeline(...).step() on every rank (pinned host buffers; each step's copies "
                   "overlap the neighbouring steps' compute)"}
+    # what bounds the end-to-end step: the device's own step, or the copy
+    # of the result to the host (all ranks share the host link)
+    e2e_ms = 1e3 * e2e_s / args.steps
+    d2h_gbs = d2h_all / (e2e_s / args.steps) / 1e9
+    e2e_limit = {"device_ms_per_step": round(ms_step, 3), "e2e_ms_per_step": round(e2e_ms, 3),
+                 "d2h_bytes_per_step_all_ranks": d2h_all, "h2d_bytes_per_step_all_ranks": h2d_all,
+                 "d2h_GBps_all_ranks": round(d2h_gbs, 1),
+                 "limited_by": ("device step" if e2e_ms < 1.1 * ms_step else
+                                "device-to-host copy of the result (the host link)")}
+
+    # weak scaling beside it (N > 1): 64 utterances on every rank
+    weak = None
+    if n > 1 and not args.no_weak:
+        rs.release()
+        rw = RankStream(args.weak_batch, args.t0, rank, dev)
+        wdt, _ = rw.device_steps(args.steps, args.warmup, barrier)
+        wdt = max_over_ranks(wdt)
+        we_dt, _, wd2h = rw.e2e_steps(args.steps, args.warmup, barrier)
+        we_dt = max_over_ranks(we_dt)
+        wd2h = int(shard.sum_over_ranks(wd2h, device=dev))
+        weak = {"batch_per_gpu": args.weak_batch, "global_batch": args.weak_batch * n,
+                "value": args.weak_batch * n * args.steps / wdt, "unit": UNIT,
+                "ms_per_step": round(1e3 * wdt / args.steps, 3),
+                "e2e": {"value": args.weak_batch * n * args.steps / we_dt, "unit": UNIT,
+                        "ms_per_step": round(1e3 * we_dt / args.steps, 3), "d2h_bytes_per_step": wd2h}}
+        rw.release()
 
     extra = {}
     if rank == 0 and n == 1 and not args.no_per_op:
+        rs.release()
         rt = BtRuntime(dev)
         extra["per_op"] = per_op(rt, torch, peak)
 
@@ -576,20 +654,23 @@ def run_b200(args):
     if do_cpu:
         procs = pool._processes
         oracle_step(pool, procs, args.t0, 0)             # warm the workers (imports)
-        dt, u = oracle_step(pool, procs, args.t0, 1)
+        dt_c, u = oracle_step(pool, procs, args.t0, 1)
         pool.close()
-        cpu = {"value": u / dt, "unit": UNIT, "cores": procs, "kind": "port",
+        cpu = {"value": u / dt_c, "unit": UNIT, "cores": procs, "kind": "port",
                "sample": f"{u} full-length utterances, one per worker process, through the numpy oracle "
                          "(oracle/ops.py, the reference's op table restated), after one warm-up round"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32", "data": DATA, "config": config(args, n),
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk, "stream_algorithmic_bytes_per_step": stream_bytes,
-                "stream_GBps_per_gpu": round(stream_bytes * args.steps / elapsed / 1e9, 1),
-                "stream_frac_of_measured": round(stream_bytes / (elapsed / args.steps) / 1e9 / peak, 4)}
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "e2e_limit": e2e_limit,
+                "gpu_launches": launches * n, "gpu_launches_per_rank": launches,
+                "clocks": clk, "stream_algorithmic_bytes_per_step": stream_bytes_all,
+                "stream_GBps_per_gpu": round(stream_bytes_all / n * args.steps / elapsed / 1e9, 1),
+                "stream_frac_of_measured": round(stream_bytes_all / n / (elapsed / args.steps) / 1e9 / peak, 4)}
+        if weak is not None:
+            line["weak"] = weak
         line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -706,7 +787,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--batch", type=int, default=64, help="utterances per GPU")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="utterances in the batch, split over the GPUs (strong scaling)")
+    ap.add_argument("--weak-batch", type=int, default=64,
+                    help="utterances per GPU of the weak-scaling figure reported beside it at N > 1")
+    ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure at N > 1")
     ap.add_argument("--t0", type=int, default=400)
     ap.add_argument("--cpu-procs", type=int, default=64)
     ap.add_argument("--no-cpu-baseline", action="store_true")

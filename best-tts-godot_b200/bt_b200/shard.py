@@ -55,6 +55,16 @@ def max_over_ranks(value, device=None):
     return float(t.item())
 
 
+def sum_over_ranks(value, device=None):
+    """Sum of a number over all ranks (bytes moved by the whole job)."""
+    world, _ = world_and_rank()
+    if world == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def barrier(device=None):
     """Barrier across ranks, then (on a GPU) a device synchronize."""
     world, _ = world_and_rank()

@@ -28,7 +28,7 @@ def _init(rank, world, port, timeout_s=60):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=timeout_s))
 
 
-def _sharded_worker(rank, world, port, per_rank, t0, result_dir):
+def _sharded_worker(rank, world, port, per_rank, t0, result_dir, total=None):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path.insert(0, here)
@@ -37,12 +37,18 @@ def _sharded_worker(rank, world, port, per_rank, t0, result_dir):
     from bt_b200.decoder import build_stream
     _init(rank, world, port)
     try:
-        start, count = shard.utterance_range(per_rank, rank)
+        # weak scaling: per_rank utterances each; strong: a fixed total split
+        if total is None:
+            start, count = shard.utterance_range(per_rank, rank)
+            total = per_rank * world
+        else:
+            start, count = shard.split_utterances(total, world, rank)
         ranges = [None] * world
         dist.all_gather_object(ranges, (start, count))
         slowest = shard.max_over_ranks(0.25 + rank)
+        assert shard.sum_over_ranks(count) == total
         # this rank's utterances, cut from the job-wide inputs
-        full = build_stream(per_rank * world, t0=t0)
+        full = build_stream(total, t0=t0)
         env_all = C.c5_small_inputs(full, seed=11)
         mine = build_stream(count, t0=t0)
         assert mine.consts.keys() == full.consts.keys()
@@ -99,26 +105,31 @@ def test_utterance_ranges_are_disjoint_and_cover():
 def test_single_process_helpers_without_a_group():
     assert shard.world_and_rank() == (1, 0)
     assert shard.max_over_ranks(2.5) == 2.5
+    assert shard.sum_over_ranks(2.5) == 2.5
     shard.barrier()
 
 
 @pytest.mark.timeout(300)
-def test_two_gloo_ranks_shard_utterances_exactly(tmp_path):
+@pytest.mark.parametrize("scaling", ["weak", "strong"])
+def test_two_gloo_ranks_shard_utterances_exactly(tmp_path, scaling):
     """Two ranks run their own utterances through the oracle; the gathered
     results equal one process running all of them, bit for bit, and the job
-    time is the slower rank's."""
+    time is the slower rank's.  weak: two utterances per rank; strong: one
+    fixed batch of three split 2 + 1 (the split bench.py --gpus N uses for
+    the BASELINE batch of 64)."""
     import sys
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     from golden import cases as C
     from oracle.ops import OracleRuntime
     from bt_b200.decoder import build_stream
     per_rank, world, t0 = 2, 2, 8
-    mp.start_processes(_sharded_worker, args=(world, _free_port(), per_rank, t0, str(tmp_path)), nprocs=world,
-                       start_method="spawn", join=True)
+    total = None if scaling == "weak" else 3
+    mp.start_processes(_sharded_worker, args=(world, _free_port(), per_rank, t0, str(tmp_path), total),
+                       nprocs=world, start_method="spawn", join=True)
     got = np.load(os.path.join(tmp_path, "sharded.npz"))
-    assert got["ranges"].tolist() == [[0, 2], [2, 2]]
+    assert got["ranges"].tolist() == ([[0, 2], [2, 2]] if total is None else [[0, 2], [2, 1]])
     assert float(got["slowest"]) == 1.25
-    full = build_stream(per_rank * world, t0=t0)
+    full = build_stream(per_rank * world if total is None else total, t0=t0)
     env = C.c5_small_inputs(full, seed=11)
     with warnings.catch_warnings():
         warnings.simplefilter("ignore")
