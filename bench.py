@@ -348,8 +348,44 @@ def per_op(rt, torch, peak):
         ms, gbs = measure_op(lambda op=op, ins=ins: rt.elementwise(op, ins, A.shape, np.float32, np.float32,
                                                                      alpha=0.2), nb, flush, 5, torch)
         sweep[nm] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    # the rest of the listed element-wise ops
+    Aabs = A.abs()
+    two = torch.tensor(2.0, device="cuda")
+    p17 = torch.tensor(1.7, device="cuda")
+    for nm, op, ins, nb in [("sub_same_shape", "SUB", [A, A2], 3 * n * 4), ("div_rowbcast", "DIV", [A, Bv],
+                                                                              2 * n * 4 + 8192 * 4),
+                            ("pow2", "POW", [A, two], 2 * n * 4 + 4), ("pow_general", "POW", [Aabs, p17], 2 * n * 4 + 4),
+                            ("sqrt", "SQRT", [Aabs], 2 * n * 4)]:
+        ms, gbs = measure_op(lambda op=op, ins=ins: rt.elementwise(op, ins, A.shape, np.float32, np.float32),
+                             nb, flush, 5, torch)
+        sweep[nm] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    del Aabs
+    # int8 weights: DequantizeLinear alone (per-row scale) and fused with the
+    # gain Mul (one pass, bt_fused_chain); Snake as one chain
+    gq8 = torch.Generator(device="cuda").manual_seed(1)
+    W8 = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda", generator=gq8)
+    sc8 = torch.rand((8192, 1), device="cuda", generator=gq8) * 0.02 + 1e-3
+    gn8 = torch.rand((8192, 1), device="cuda", generator=gq8) + 0.5
+    ms, gbs = measure_op(lambda: rt.elementwise("DEQUANT", [W8, sc8], W8.shape, np.float32, np.float32),
+                         n * 5 + 8192 * 4, flush, 5, torch)
+    sweep["dequant_int8"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
+    ms, gbs = measure_op(lambda: rt.dequant_mul(W8, sc8, None, gn8), n * 5 + 8192 * 8, flush, 5, torch)
+    sweep["dequant_int8_x_gain_chain"] = {"ms": round(ms, 4), "GBps": round(gbs, 1),
+                                          "frac_of_measured": round(gbs / peak, 4), "launches": 1}
+    del W8
+    A3s = A.reshape(64, 128, 8192)
+    al8 = (torch.rand((1, 128, 1), device="cuda", generator=gq8) + 0.5).half()
+    ial8 = (1.0 / al8.float()).half()
+    two16 = torch.tensor(2.0, device="cuda").half()
+    ms, gbs = measure_op(lambda: rt.snake(A3s, al8, ial8, two16), 2 * n * 4 + 128 * 4, flush, 5, torch)
+    sweep["snake_chain"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4),
+                            "launches": 1}
     gl = torch.rand(768, device="cuda")
     Al = A.reshape(-1)[: (n // 768) * 768].reshape(-1, 768)
+    Al2 = A2.reshape(-1)[: (n // 768) * 768].reshape(-1, 768)
+    ms, gbs = measure_op(lambda: rt.layernorm(Al, Al2, None, gl, gl, -1, 1e-12), 3 * Al.numel() * 4 + 6144,
+                         flush, 5, torch)
+    sweep["skip_layernorm_768"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt.layernorm(Al, None, None, gl, None, -1, 1e-5), 2 * Al.numel() * 4 + 3072,
                          flush, 5, torch)
     sweep["layernorm_768"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
@@ -722,7 +758,8 @@ def run_profile_adain(args):
 
 
 PROFILE_OPS = ("reducemean_c2", "softmax_c3_b16", "layernorm_768", "reducemean_8192", "dynquant_256MB",
-               "conv_epilogue_256MB", "transpose_256MB", "tanh_256MB", "adain_dq_256MB")
+               "conv_epilogue_256MB", "transpose_256MB", "tanh_256MB", "adain_dq_256MB", "dequant_gain_320MB",
+               "snake_512MB")
 
 
 def run_profile_op(args):
@@ -731,9 +768,11 @@ def run_profile_op(args):
     (c3 masked softmax at batch 16) or 'layernorm_768' (LayerNormalization
     over 768 channels of a 256 MB tensor); the 256 MB sweep's
     'reducemean_8192', 'dynquant_256MB', 'conv_epilogue_256MB',
-    'transpose_256MB' ([64,128,8192] -> [64,8192,128]), 'tanh_256MB' and
+    'transpose_256MB' ([64,128,8192] -> [64,8192,128]), 'tanh_256MB',
     'adain_dq_256MB' (AdaIN+Snake with the range folded in, then the
-    quantize pass)."""
+    quantize pass), 'dequant_gain_320MB' (int8 [8192, 8192] dequantised
+    and scaled in one chain) and 'snake_512MB' (Snake as one chain over
+    [64, 128, 8192])."""
     import torch
     from bt_b200 import configs
     from bt_b200.runtime import BtRuntime
@@ -751,6 +790,15 @@ def run_profile_op(args):
         A = torch.randn((64 * 1024 * 1024 // 768, 768), device="cuda")
         g = torch.rand(768, device="cuda")
         fn = lambda: rt.layernorm(A, None, None, g, None, -1, 1e-5)
+    elif name == "dequant_gain_320MB":
+        W8 = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        sc, gn = torch.rand((8192, 1), device="cuda") * 0.02, torch.rand((8192, 1), device="cuda") + 0.5
+        fn = lambda: rt.dequant_mul(W8, sc, None, gn)
+    elif name == "snake_512MB":
+        X = torch.randn((64, 128, 8192), device="cuda")
+        al = (torch.rand((1, 128, 1), device="cuda") + 0.5).half()
+        ial, two = (1.0 / al.float()).half(), torch.tensor(2.0, device="cuda").half()
+        fn = lambda: rt.snake(X, al, ial, two)
     else:
         A = torch.randn((64, 128, 8192), device="cuda")
         if name == "reducemean_8192":

@@ -83,6 +83,7 @@ SIGNATURES = {
     "bt_sync": (ctypes.c_int, []),
     "bt_elementwise": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P(BtTensor), _P(BtTensor), _P(BtEwAttrs)]),
     "bt_fused_chain": (ctypes.c_int, [_P(BtChain), _P(BtTensor), _P(BtTensor)]),
+    "bt_chain_kind": (ctypes.c_int, [_P(BtChain)]),
     "bt_reduce": (ctypes.c_int, [ctypes.c_int, _P(BtTensor), _P(ctypes.c_int64), ctypes.c_int, ctypes.c_int,
                                  _P(BtTensor)]),
     "bt_softmax": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_int, _P(BtTensor)]),

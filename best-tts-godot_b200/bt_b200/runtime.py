@@ -64,6 +64,7 @@ _UNARY_NP = {"Sqrt": np.sqrt, "Exp": np.exp, "Sin": np.sin, "Cos": np.cos, "Atan
              "Tanh": np.tanh, "Sigmoid": lambda v: 1.0 / (1.0 + np.exp(-v)), "Floor": np.floor,
              "Round": np.rint, "Erf": None}
 COMPARE = {"Greater": "GREATER", "Less": "LESS", "GreaterOrEqual": "GEQ"}
+_F16_TWO = np.array(2.0, dtype=np.float16)   # the Snake exponent constant of the graph
 
 
 def as_cuda_device(device):
@@ -488,11 +489,40 @@ class BtRuntime:
             raise NotImplementedError(f"{op} ({node_output}) is not on the B200 path")
         env[node_output[0]] = out
 
-    def run_nodes(self, nodes, env):
+    def run_nodes(self, nodes, env, fuse=False, keep=()):
         """Executes ``(op, inputs, outputs, attrs)`` nodes in order, wrapping
-        failures like the reference's drivers (ref_runtime.py:398-403)."""
-        for op, ins, outs, at in nodes:
+        failures like the reference's drivers (ref_runtime.py:398-403).
+
+        fuse: runs of nodes that form a known chain (Snake, DequantizeLinear
+        then Mul, Add then Sigmoid / LeakyRelu, Mul then Add; chains.plan)
+        run as one bt_fused_chain launch each, with identical results; their
+        intermediate values are then not stored in ``env``.  A value read by
+        more than one node, or named in ``keep``, is never fused away."""
+        groups = {}
+        skip = set()
+        if fuse:
+            from . import chains
+            for g in chains.plan(nodes, keep):
+                groups[g.last] = g
+                skip.update(g.nodes)
+        for i, (op, ins, outs, at) in enumerate(nodes):
             try:
+                g = groups.get(i)
+                if g is not None:
+                    vals = [env[n] if n else None for n in g.inputs]
+                    dts = [np_dtype(v) if isinstance(v, torch.Tensor) else np.asarray(v).dtype for v in vals]
+                    ins_dev = [self.to_device(v) for v in vals] if g.inputs_ok(dts) else None
+                    # (a view input would give numpy's result its own axis
+                    # order, which later reductions follow: node by node then)
+                    if ins_dev is not None and all(t.is_contiguous() for t in ins_dev):
+                        env[g.output] = self.chain(g.prog(), ins_dev)
+                        continue
+                    for j in g.nodes:   # not a float32 chain: node by node
+                        jop, jins, jouts, jat = nodes[j]
+                        self.dispatch(jop, list(jins), list(jouts), dict(jat or {}), env)
+                    continue
+                if i in skip:
+                    continue
                 self.dispatch(op, list(ins), list(outs), dict(at or {}), env)
             except Exception as exc:
                 raise RuntimeError(f"{op} {list(outs)} failed: {exc}") from exc
@@ -753,8 +783,12 @@ class BtRuntime:
         return y.permute(inv)
 
     # ---- fused entry points (beyond the one-op-per-node table) ---------------------
-    def chain(self, prog, inputs, out_shape):
-        """Runs a bt_chain register program (float32) over broadcast inputs."""
+    def chain(self, prog, inputs, out_shape=None):
+        """Runs a bt_chain register program (float32, see bt_fused_chain)
+        over CUDA tensors broadcast to out_shape (default: their broadcast
+        shape); one launch, a dense float32 result."""
+        if out_shape is None:
+            out_shape = np.broadcast_shapes(*[tuple(t.shape) for t in inputs])
         out = self._empty(out_shape, np.float32)
         if out.numel() == 0:
             return out
@@ -767,12 +801,29 @@ class BtRuntime:
     def dequant_mul(self, q, scale, zero_point, gain):
         """Mul(DequantizeLinear(q, scale, zero_point), gain): the c4 weight
         path, rounded like the two reference ops (ref_runtime.py:631-636
-        then :450-451) -- two library launches."""
+        then :450-451).  One pass reading the int8 weights (bt_fused_chain)
+        where the two ops compute in float32: q and zero point int8 / uint8,
+        scale and gain float32 / float16; otherwise the two ops one after
+        the other."""
+        from . import chains
+        g = chains.FusedGroup(0, 1, "dequant_mul", [], "", quant=(0, 3))
+        ins = [q, scale, gain] + ([zero_point] if zero_point is not None else [])
+        if g.inputs_ok([np_dtype(t) for t in ins]):
+            return self.chain(chains.dequant_mul_program(zero_point is not None), ins)
         ins = [q, scale] + ([zero_point] if zero_point is not None else [])
         shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
         d = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
         shape2 = np.broadcast_shapes(shape, tuple(gain.shape))
         return self.elementwise("MUL", [d, self._as_f32(gain)], shape2, np.float32, np.float32)
+
+    def snake(self, x, alpha, inv_alpha, power=None):
+        """Snake x + inv_alpha * sin(alpha * x) ** power as the graph spells
+        it (Mul, Sin, Pow, Mul, Add; power defaults to the graph's float16
+        2.0), in one pass (bt_fused_chain); float32 / float16 inputs."""
+        from . import chains
+        if power is None:
+            power = self.to_device(_F16_TWO)
+        return self.chain(chains.snake_program(), [x, alpha, power, inv_alpha])
 
     def adain_snake(self, srcs, gain, shift, eps, alpha=None, inv_alpha=None, res=None, outs=None,
                     ranges=None):

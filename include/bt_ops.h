@@ -118,21 +118,32 @@ int bt_elementwise(int op, int n_in, const bt_tensor* in, const bt_tensor* out,
                    const bt_ew_attrs* attrs);
 
 /* Fused elementwise chain: a short register program evaluated per element of
- * the broadcast iteration space, each instruction rounding in fp32 as the
- * separate numpy ops would (no contraction).  Inputs are loaded (fp16/int8/
- * int32 widened to fp32) into registers r0..r(n_in-1); instruction k writes
- * register dst.  The output is register `out_reg`.
+ * the broadcast iteration space of its inputs, in one pass (every input read
+ * once at its stored type, the float32 result written once).  Inputs are
+ * widened to float32 into registers r0..r(n_in-1); instruction k computes
+ * dst = op(a, b) in float32, rounding once as the numpy op it stands for
+ * would (no contraction); the result is register `out_reg`.  Input dtypes:
+ * float32, float16, int8, uint8, int16, uint16, bool (their float32 widening
+ * is exact, so float32 arithmetic is numpy's arithmetic next to float32
+ * data).  The output is dense float32 of the broadcast shape.  A register
+ * read before it was written, an unknown op or a bad register index is
+ * BT_EINVAL; more than 2^32 - 1 rows (all axes but the last merged one) is
+ * BT_ETOOBIG.
+ * Programs of the built-in catalog (bt_chain_kind) run in kernels compiled
+ * for them; every other valid program runs in an interpreter kernel (the
+ * same results, more instructions per value).
  * replaces: chains of ref_runtime.py:446-479 dispatches such as Snake
- *           (Mul, Sin, Pow 2, Mul, Add) and dequant + gain, each of which the
- *           reference executes as a separate dispatch with a barrier
- *           (executor.gd:696-698). */
+ *           (Mul, Sin, Pow 2, Mul, Add) and DequantizeLinear + gain Mul
+ *           (:631-636, :450-451), each of which the reference executes as a
+ *           separate dispatch with a barrier (executor.gd:678-699, the
+ *           two-dispatch DequantizeLinear at :822-827). */
 #define BT_CHAIN_MAX_INSTR 16
 #define BT_CHAIN_MAX_IN 6
 typedef struct bt_chain_instr {
   int32_t op;        /* bt_op among ADD SUB MUL DIV POW SQRT EXP SIN COS TANH
                         SIGMOID LEAKYRELU ERF IDENTITY NEG ABS MIN MAX FLOOR
                         ROUND ATAN */
-  int32_t dst, a, b; /* register indices (b unused by unary ops) */
+  int32_t dst, a, b; /* register indices 0..15 (b unused by unary ops) */
   float   alpha;     /* LeakyRelu slope */
 } bt_chain_instr;
 typedef struct bt_chain {
@@ -143,6 +154,22 @@ typedef struct bt_chain {
 } bt_chain;
 int bt_fused_chain(const bt_chain* prog, const bt_tensor* in,
                    const bt_tensor* out);
+/* Which kernel bt_fused_chain runs for `prog` (host only): the index of the
+ * catalog entry it matches once its registers are renamed to
+ * single-assignment form, BT_CHAIN_INTERPRETER for the interpreter, or a
+ * negative BT_E* code for an invalid program.  Catalog, in order, with the
+ * inputs in the order given:
+ *   0 Mul(DequantizeLinear(q, scale), gain)             inputs q, scale, gain
+ *   1 Mul(DequantizeLinear(q, scale, zp), gain)         inputs q, scale, gain, zp
+ *   2 Snake x + inv_alpha * sin(alpha * x) ** p          inputs x, alpha, p, inv_alpha
+ *     (the graph's Mul, Sin, Pow, Mul, Add)
+ *   3 Sigmoid(Add(x, y))                                inputs x, y
+ *   4 Add(Mul(x, g), b)                                 inputs x, g, b
+ *   5 LeakyRelu(Add(x, y))                              inputs x, y
+ * replaces: nothing in the reference (a query about this library's own
+ *           kernels). */
+#define BT_CHAIN_INTERPRETER 64
+int bt_chain_kind(const bt_chain* prog);
 
 /* ---- reductions --------------------------------------------------------
  * kind: 0 = ReduceSum, 1 = ReduceMean.  `axes` are normalised axes of x

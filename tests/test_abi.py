@@ -166,17 +166,52 @@ def test_host_pairwise_sum_is_numpy_exact(lib, n):
     assert got.view(np.uint32) == want.view(np.uint32)
 
 
-def test_fused_chain_validates_then_reports_withdrawn(lib):
-    """The register-program entry point validates its arguments and then
-    reports that its kernel is withdrawn (it faulted on the B200)."""
+def test_fused_chain_validates_programs(lib):
+    """bt_fused_chain rejects malformed programs before touching the GPU:
+    bad header, unknown op, register out of range, a register read before
+    anything wrote it, an output register never written."""
+    from bt_b200 import chains
+    x = _lib.make_tensor(0x1000, np.float32, (4,))
+    one = (_lib.BtTensor * 1)(x)
+
+    def status(prog):
+        return lib.bt_fused_chain(ctypes.byref(prog), one, ctypes.byref(x)), lib.bt_chain_kind(ctypes.byref(prog))
+
     prog = _lib.BtChain()
     prog.n_in = 0
-    x = _lib.make_tensor(0x1000, np.float32, (4,))
-    assert lib.bt_fused_chain(ctypes.byref(prog), (_lib.BtTensor * 1)(x), ctypes.byref(x)) == -1
-    prog.n_in, prog.n_instr, prog.out_reg = 1, 1, 1
-    prog.instr[0] = _lib.BtChainInstr(0, 1, 0, 0, 0.0)
-    assert lib.bt_fused_chain(ctypes.byref(prog), (_lib.BtTensor * 1)(x), ctypes.byref(x)) == -5
-    assert b"withdrawn" in lib.bt_last_error()
+    assert status(prog) == (-1, -1)
+    assert status(chains.program(1, [("ADD", 1, 0, 5)], 1)) == (-1, -1)         # r5 never written
+    assert status(chains.program(1, [("ADD", 16, 0, 0)], 16)) == (-1, -1)       # register 16
+    assert status(chains.program(1, [("WHERE", 1, 0, 0)], 1)) == (-1, -1)       # not a chain op
+    assert status(chains.program(1, [("SIN", 1, 0, 0)], 2)) == (-1, -1)         # output never written
+    assert b"never written" in lib.bt_last_error()
+    bad = chains.program(1, [("ADD", 1, 0, 0)], 1)
+    bad.instr[0].op = 99
+    assert status(bad) == (-1, -1)
+
+
+def test_chain_catalog_kinds(lib):
+    """Programs are matched to the compiled catalog after renaming their
+    registers to single-assignment form, so register reuse does not matter;
+    any other valid program goes to the interpreter."""
+    from bt_b200 import chains
+    kind = lambda p: lib.bt_chain_kind(ctypes.byref(p))   # noqa: E731
+    assert kind(chains.dequant_mul_program(False)) == 0
+    assert kind(chains.dequant_mul_program(True)) == 1
+    assert kind(chains.snake_program()) == 2
+    assert kind(chains.add_unary_program("SIGMOID")) == 3
+    assert kind(chains.mul_add_program()) == 4
+    assert kind(chains.add_unary_program("LEAKYRELU", 0.1)) == 5
+    # Snake written with fresh registers for every step: the same program
+    fresh = chains.program(4, [("MUL", 4, 1, 0), ("SIN", 5, 4, 4), ("POW", 6, 5, 2), ("MUL", 7, 3, 6),
+                               ("ADD", 8, 0, 7)], 8)
+    assert kind(fresh) == 2
+    # overwriting an input register is allowed (single-assignment renaming)
+    assert kind(chains.program(2, [("ADD", 0, 0, 1), ("SIGMOID", 0, 0, 0)], 0)) == 3
+    # other programs: the interpreter
+    assert kind(chains.program(2, [("SUB", 2, 0, 1), ("EXP", 2, 2, 2)], 2)) == 64
+    assert kind(chains.program(2, [("ADD", 2, 1, 0), ("SIGMOID", 2, 2, 2)], 2)) == 64   # operands swapped
+    assert kind(chains.program(1, [], 0)) == 64
 
 
 @pytest.mark.gpu
