@@ -901,12 +901,12 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
     int head = (4 - phase4(b)) & 3;
     if (head > n) head = n;
     const int nvec = (n - head) >> 2, tail0 = head + 4 * nvec;
-    const bool mvec = mr && a.mask_col_st && phase4(mr) == phase4(b);
+    const bool mvec = mr && a.mask_col_st == 1 && phase4(mr) == phase4(b);
     float m = -INFINITY;
     if (mr && a.mask_col_st) {
       for (int i = lane; i < n; i += 32) {
         if (mvec && i >= head && i < tail0) continue;
-        const float v = BT_ADD(b[i], mr[i]);
+        const float v = BT_ADD(b[i], mr[i * a.mask_col_st]);
         b[i] = v;
         m = fmaxf(m, v);
       }
@@ -956,6 +956,138 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
     const double rd = recip_d(denom);
     warp_write(a.out + row * (int64_t)n, b, x + row * (int64_t)n, n, [=](float v, int) { return div_by(v, rd); });
   });
+}
+
+// ---- register-resident softmax rows ------------------------------------------
+// Softmax over rows of a compile-time length N (even, at most 512; ALBERT's
+// 510-key attention rows): one warp per row, the row held in registers.
+// Lane l = 4G + p (group G of four lanes, position p) holds, in slot k, the
+// pair of elements 64G + 8k + 2p and +1: the eight values of block
+// b = 8G + k (elements 8b .. 8b + 7) sit in the four lanes of group G, two
+// each, which is the layout of numpy's eight pairwise accumulators.  numpy's
+// tree over the row (pw_split) is unrolled at compile time: a leaf's
+// accumulator pairs run down its blocks within a group (one two-lane add per
+// block) and hop to the next group with one shuffle; the bracket
+// ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) is two shuffles; the leftover values
+// of a leaf are gathered in order.  No shared memory, no loop over leaves,
+// no plan: every index is a constant.
+__host__ __device__ constexpr int pw_split_c(int n) { return n / 2 - (n / 2) % 8; }
+
+// numpy's sum of the leaf [OFF, OFF + LEN) (OFF a multiple of 8), the same
+// value in every lane.
+template <int LEN, int OFF>
+__device__ __forceinline__ float reg_leaf_sum(const float2 (&v)[8]) {
+  constexpr int b0 = OFF / 8, nb = LEN / 8, R = LEN % 8;
+  float res = 0.0f;                       // a run shorter than 8 starts from +0.0
+  if constexpr (nb > 0) {
+    float2 acc = v[b0 % 8];               // r[j] = a[j] (held by group b0 / 8)
+#pragma unroll
+    for (int b = b0 + 1; b < b0 + nb; ++b) {
+      if (b % 8 == 0) {                   // the next block sits in the next group
+        acc.x = __shfl_up_sync(0xffffffffu, acc.x, 4);
+        acc.y = __shfl_up_sync(0xffffffffu, acc.y, 4);
+      }
+      acc = pk_add(acc, v[b % 8]);
+    }
+    float t = BT_ADD(acc.x, acc.y);
+    t = BT_ADD(t, __shfl_xor_sync(0xffffffffu, t, 1));
+    t = BT_ADD(t, __shfl_xor_sync(0xffffffffu, t, 2));
+    res = __shfl_sync(0xffffffffu, t, 4 * ((b0 + nb - 1) / 8));
+  }
+  if constexpr (R > 0) {
+    constexpr int bR = b0 + nb;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const float c = (i & 1) ? v[bR % 8].y : v[bR % 8].x;
+      res = BT_ADD(res, __shfl_sync(0xffffffffu, c, 4 * (bR / 8) + (i >> 1)));
+    }
+  }
+  return res;
+}
+
+template <int LEN, int OFF>
+__device__ __forceinline__ float reg_pw_sum(const float2 (&v)[8]) {
+  if constexpr (LEN <= kPwLeaf) {
+    return reg_leaf_sum<LEN, OFF>(v);
+  } else {
+    constexpr int S = pw_split_c(LEN);
+    const float l = reg_pw_sum<S, OFF>(v);
+    const float r = reg_pw_sum<LEN - S, OFF + S>(v);
+    return BT_ADD(l, r);
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
+  static_assert(N % 2 == 0 && N >= 2 && N <= 512, "rows of an even length up to 512");
+  const int lane = threadIdx.x & 31;
+  const int e0 = 64 * (lane >> 2) + 2 * (lane & 3);   // element of slot 0
+  // a mask shared by every row is read once
+  float2 mk[8];
+  const bool mconst = a.mask && a.mask_row_const;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int e = e0 + 8 * k;
+    mk[k] = make_float2(0.0f, 0.0f);
+    if (mconst && e < N) mk[k] = make_float2(a.mask[e * a.mask_col_st], a.mask[(e + 1) * a.mask_col_st]);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    const float* xr = a.x + row * N;
+    float2 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = e0 + 8 * k;
+      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
+    }
+    if (a.mask) {
+      if (mconst) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (e0 + 8 * k < N) v[k] = pk_add(v[k], mk[k]);
+      } else {
+        // this row's mask row (32-bit unravel: the host sends fewer than 2^32 rows)
+        long long moff = 0;
+        if (lane == 0) {
+          uint32_t rem = (uint32_t)row;
+          for (int d = a.lead_rank - 1; d >= 0; --d) {
+            const uint32_t ext = (uint32_t)a.lead_shape[d];
+            const uint32_t c = rem % ext;
+            rem /= ext;
+            moff += (long long)c * a.mask_lead_st[d];
+          }
+        }
+        moff = __shfl_sync(0xffffffffu, moff, 0);
+        const float* mr = a.mask + moff;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int e = e0 + 8 * k;
+          if (e < N) v[k] = pk_add(v[k], make_float2(mr[e * a.mask_col_st], mr[(e + 1) * a.mask_col_st]));
+        }
+      }
+    }
+    // row maximum (a NaN anywhere makes the whole row NaN either way, see
+    // wrow_softmax_kernel)
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = fmaxf(m, fmaxf(v[k].x, v[k].y));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    // exp(x - max), two lanes per instruction (x - m == x + (-m))
+    const float2 nm = pk(-m);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (e0 + 8 * k < N) v[k] = pk_np_exp(pk_add(v[k], nm));
+    const float total = reg_pw_sum<N, 0>(v);
+    const float denom = BT_ADD(0.0f, total);
+    const double rd = recip_d(denom);
+    float* orow = a.out + row * N;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int e = e0 + 8 * k;
+      if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
+    }
+  }
 }
 
 __global__ void __launch_bounds__(256) wrow_layernorm_kernel(WLayerNormArgs A) {
@@ -1489,6 +1621,18 @@ extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, c
     a.mask_row_const = 1;
     for (int d = 0; d < a.lead_rank; ++d)
       if (a.mask_lead_st[d] != 0) a.mask_row_const = 0;
+  }
+  // rows of 510 / 512 values, 8-byte aligned: held in registers
+  if ((n == 510 || n == 512) && rows < (1ll << 32) && ((uintptr_t)x->data & 7) == 0 &&
+      ((uintptr_t)out->data & 7) == 0) {
+    DevInfo di;
+    const int sms = (dev_info(&di) == BT_OK && di.sm_count > 0) ? di.sm_count : 148;
+    const int64_t need = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+    const int64_t cap = (int64_t)sms * 8;   // 8 CTAs of 8 warps per SM at most
+    const int grid = (int)(need < cap ? need : cap);
+    if (n == 510) wrow_softmax_reg_kernel<510><<<grid, 32 * kWarpsPerCta, 0, cur_stream()>>>(a);
+    else wrow_softmax_reg_kernel<512><<<grid, 32 * kWarpsPerCta, 0, cur_stream()>>>(a);
+    return check_launch("bt_softmax(register rows)");
   }
   WPlan wp;
   if (n <= kWarpRowMax && rows < (1ll << 32) && wplan_for((int)n, &wp)) {
