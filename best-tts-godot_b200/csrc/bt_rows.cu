@@ -958,68 +958,88 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
   });
 }
 
-// ---- register-resident softmax rows ------------------------------------------
-// Softmax over rows of a compile-time length N (even, at most 512; ALBERT's
-// 510-key attention rows): one warp per row, the row held in registers.
-// Lane l = 4G + p (group G of four lanes, position p) holds, in slot k, the
-// pair of elements 64G + 8k + 2p and +1: the eight values of block
-// b = 8G + k (elements 8b .. 8b + 7) sit in the four lanes of group G, two
-// each, which is the layout of numpy's eight pairwise accumulators.  numpy's
-// tree over the row (pw_split) is unrolled at compile time: a leaf's
-// accumulator pairs run down its blocks within a group (one two-lane add per
-// block) and hop to the next group with one shuffle; the bracket
+// ---- register-resident rows -----------------------------------------------------
+// Rows of a compile-time length N (softmax over ALBERT's 510-key attention
+// rows, layer norm over its 768 channels): one warp per row, the row held in
+// registers.  Lane l = 4G + p (group G of four lanes, position p) holds, in
+// slot k < NS, the pair of elements 8b + 2p and +1 of block b = NS G + k:
+// the eight values of a block sit in the four lanes of one group, two each,
+// which is the layout of numpy's eight pairwise accumulators.  numpy's tree
+// over the row (pw_split) is unrolled at compile time: a leaf's accumulator
+// pairs run down its blocks within a group (one two-lane add per block) and
+// hop to the next group with one shuffle; the bracket
 // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) is two shuffles; the leftover values
 // of a leaf are gathered in order.  No shared memory, no loop over leaves,
 // no plan: every index is a constant.
 __host__ __device__ constexpr int pw_split_c(int n) { return n / 2 - (n / 2) % 8; }
 
-// numpy's sum of the leaf [OFF, OFF + LEN) (OFF a multiple of 8), the same
-// value in every lane.
-template <int LEN, int OFF>
-__device__ __forceinline__ float reg_leaf_sum(const float2 (&v)[8]) {
+struct RegIdentity {
+  __device__ __forceinline__ float2 operator()(float2 v) const { return v; }
+};
+// (v - mu)^2 of both lanes, each step rounded on its own (numpy's x - mu,
+// then ** 2, which is x * x)
+struct RegSquaredDev {
+  float mu;
+  __device__ __forceinline__ float2 operator()(float2 v) const {
+    const float dx = BT_SUB(v.x, mu), dy = BT_SUB(v.y, mu);
+    return make_float2(BT_MUL(dx, dx), BT_MUL(dy, dy));
+  }
+};
+
+// numpy's sum of f(values) over the leaf [OFF, OFF + LEN) (OFF a multiple of
+// 8), the same value in every lane.
+template <int NS, int LEN, int OFF, class F>
+__device__ __forceinline__ float reg_leaf_sum(const float2 (&v)[NS], F f) {
   constexpr int b0 = OFF / 8, nb = LEN / 8, R = LEN % 8;
   float res = 0.0f;                       // a run shorter than 8 starts from +0.0
   if constexpr (nb > 0) {
-    float2 acc = v[b0 % 8];               // r[j] = a[j] (held by group b0 / 8)
+    float2 acc = f(v[b0 % NS]);           // r[j] = a[j] (held by group b0 / NS)
 #pragma unroll
     for (int b = b0 + 1; b < b0 + nb; ++b) {
-      if (b % 8 == 0) {                   // the next block sits in the next group
+      if (b % NS == 0) {                  // the next block sits in the next group
         acc.x = __shfl_up_sync(0xffffffffu, acc.x, 4);
         acc.y = __shfl_up_sync(0xffffffffu, acc.y, 4);
       }
-      acc = pk_add(acc, v[b % 8]);
+      const float2 t = f(v[b % NS]);
+      acc = make_float2(BT_ADD(acc.x, t.x), BT_ADD(acc.y, t.y));
     }
     float t = BT_ADD(acc.x, acc.y);
     t = BT_ADD(t, __shfl_xor_sync(0xffffffffu, t, 1));
     t = BT_ADD(t, __shfl_xor_sync(0xffffffffu, t, 2));
-    res = __shfl_sync(0xffffffffu, t, 4 * ((b0 + nb - 1) / 8));
+    res = __shfl_sync(0xffffffffu, t, 4 * ((b0 + nb - 1) / NS));
   }
   if constexpr (R > 0) {
     constexpr int bR = b0 + nb;
+    const float2 w = f(v[bR % NS]);
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-      const float c = (i & 1) ? v[bR % 8].y : v[bR % 8].x;
-      res = BT_ADD(res, __shfl_sync(0xffffffffu, c, 4 * (bR / 8) + (i >> 1)));
+      const float c = (i & 1) ? w.y : w.x;
+      res = BT_ADD(res, __shfl_sync(0xffffffffu, c, 4 * (bR / NS) + (i >> 1)));
     }
   }
   return res;
 }
 
-template <int LEN, int OFF>
-__device__ __forceinline__ float reg_pw_sum(const float2 (&v)[8]) {
+template <int NS, int LEN, int OFF, class F>
+__device__ __forceinline__ float reg_pw_sum(const float2 (&v)[NS], F f) {
   if constexpr (LEN <= kPwLeaf) {
-    return reg_leaf_sum<LEN, OFF>(v);
+    return reg_leaf_sum<NS, LEN, OFF>(v, f);
   } else {
     constexpr int S = pw_split_c(LEN);
-    const float l = reg_pw_sum<S, OFF>(v);
-    const float r = reg_pw_sum<LEN - S, OFF + S>(v);
+    const float l = reg_pw_sum<NS, S, OFF>(v, f);
+    const float r = reg_pw_sum<NS, LEN - S, OFF + S>(v, f);
     return BT_ADD(l, r);
   }
 }
 
+// Slots per lane for rows of N values.
+template <int N>
+__host__ __device__ constexpr int reg_slots() { return ((N + 7) / 8 + 7) / 8; }
+
 template <int N>
 __global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
   static_assert(N % 2 == 0 && N >= 2 && N <= 512, "rows of an even length up to 512");
+  static_assert(reg_slots<N>() == 8, "eight slots per lane");
   const int lane = threadIdx.x & 31;
   const int e0 = 64 * (lane >> 2) + 2 * (lane & 3);   // element of slot 0
   // a mask shared by every row is read once
@@ -1078,7 +1098,7 @@ __global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       if (e0 + 8 * k < N) v[k] = pk_np_exp(pk_add(v[k], nm));
-    const float total = reg_pw_sum<N, 0>(v);
+    const float total = reg_pw_sum<8, N, 0>(v, RegIdentity());
     const float denom = BT_ADD(0.0f, total);
     const double rd = recip_d(denom);
     float* orow = a.out + row * N;
@@ -1086,6 +1106,63 @@ __global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
     for (int k = 0; k < 8; ++k) {
       const int e = e0 + 8 * k;
       if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
+    }
+  }
+}
+
+// (Skip +) layer norm over rows of N values held in registers (see the
+// register-resident rows above): numpy's mean, then the mean of the squared
+// deviations, each a pairwise sum unrolled at compile time; the output steps
+// Sub -> Div -> Mul(gamma) [-> Add(beta)], each rounded.
+template <int N>
+__global__ void __launch_bounds__(256) wrow_layernorm_reg_kernel(LayerNormArgs a) {
+  constexpr int NS = reg_slots<N>();
+  static_assert(N % 8 == 0 && NS <= 12, "rows of a multiple of 8 values, at most 768");
+  const int lane = threadIdx.x & 31;
+  const int e0 = 8 * NS * (lane >> 2) + 2 * (lane & 3);   // element of slot 0
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    const float* xr = a.x + row * N;
+    float2 v[NS];
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      const int e = e0 + 8 * k;
+      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(0.0f, 0.0f);
+    }
+    if (a.skip || a.bias) {
+      const float* sk = a.skip ? a.skip + row * N : nullptr;
+#pragma unroll
+      for (int k = 0; k < NS; ++k) {
+        const int e = e0 + 8 * k;
+        if (e < N) {
+          if (sk) {
+            const float2 w = __ldcs(reinterpret_cast<const float2*>(sk + e));
+            v[k] = make_float2(BT_ADD(v[k].x, w.x), BT_ADD(v[k].y, w.y));
+          }
+          if (a.bias) v[k] = make_float2(BT_ADD(v[k].x, a.bias[e]), BT_ADD(v[k].y, a.bias[e + 1]));
+        }
+      }
+    }
+    const float sum = reg_pw_sum<NS, N, 0>(v, RegIdentity());
+    const float mu = np_mean_from_sum(BT_ADD(0.0f, sum), N);
+    const float ssq = reg_pw_sum<NS, N, 0>(v, RegSquaredDev{mu});
+    const float var = np_mean_from_sum(BT_ADD(0.0f, ssq), N);
+    const float sd = BT_SQRT(BT_ADD(var, a.eps));
+    const double rsd = recip_d(sd);
+    float* orow = a.out + row * N;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      const int e = e0 + 8 * k;
+      if (e < N) {
+        const float g0 = ldf(a.gamma, a.gdt, e), g1 = ldf(a.gamma, a.gdt, e + 1);
+        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), g0);
+        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), g1);
+        if (a.beta) {
+          y0 = BT_ADD(y0, ldf(a.beta, a.bdt, e));
+          y1 = BT_ADD(y1, ldf(a.beta, a.bdt, e + 1));
+        }
+        __stcs(reinterpret_cast<float2*>(orow + e), make_float2(y0, y1));
+      }
     }
   }
 }
@@ -1708,6 +1785,16 @@ extern "C" int bt_layernorm(const bt_tensor* x, const bt_tensor* skip, const bt_
     int grid;
     rc = wrow_setup((int)n, rows, &smem, &grid);
     if (rc == BT_OK) {
+      // rows of 768 values (ALBERT's hidden size), 8-byte aligned: held in registers
+      if (n == 768 && ((uintptr_t)a.x & 7) == 0 && ((uintptr_t)a.out & 7) == 0 &&
+          (!a.skip || ((uintptr_t)a.skip & 7) == 0)) {
+        DevInfo di;
+        const int sms = (dev_info(&di) == BT_OK && di.sm_count > 0) ? di.sm_count : 148;
+        const int64_t need = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
+        const int64_t cap = (int64_t)sms * 8;
+        wrow_layernorm_reg_kernel<768><<<(int)(need < cap ? need : cap), 32 * kWarpsPerCta, 0, cur_stream()>>>(a);
+        return check_launch("bt_layernorm(register rows)");
+      }
       WLayerNormArgs w{wp, a};
       wrow_layernorm_kernel<<<grid, 32 * kWarpsPerCta, smem, cur_stream()>>>(w);
       return check_launch("bt_layernorm(warp rows)");

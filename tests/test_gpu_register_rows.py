@@ -1,4 +1,5 @@
-"""Softmax over rows of 510 and 512 values (ALBERT's attention rows), which
+"""Rows held in registers: softmax over rows of 510 and 512 values (ALBERT's
+attention rows) and layer norm over 768 channels (its hidden size), which
 the register-resident kernel serves: numpy's pairwise sum unrolled at compile
 time, bit-exact against the oracle's Add + Softmax for every mask layout the
 kernel reads (one mask row for all rows, one per batch, a scalar, a strided
@@ -71,3 +72,48 @@ def test_misaligned_rows_take_the_staged_kernel(gpu_runtime):
     assert xv.data_ptr() % 8 == 4
     got = gpu_runtime.softmax(xv, None, -1)
     assert_same(got.cpu().numpy(), _oracle(x, None), "softmax of a 4-byte-offset input")
+
+
+def _oracle_ln(x, skip, bias, gamma, beta, eps):
+    env = {"x": x, "g": gamma}
+    if skip is not None:
+        env.update({"s": skip})
+        ins = ["x", "s", "g", "b" if beta is not None else "", "bi" if bias is not None else ""]
+        op, at = "SkipLayerNormalization", {"epsilon": eps}
+    else:
+        ins = ["x", "g"] + (["b"] if beta is not None else [])
+        op, at = "LayerNormalization", {"epsilon": eps, "axis": -1}
+    if beta is not None:
+        env["b"] = beta
+    if bias is not None:
+        env["bi"] = bias
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        OracleRuntime().run_nodes([(op, ins, ["y"], at)], env)
+    return env["y"]
+
+
+@pytest.mark.parametrize("variant", ["plain", "beta", "skip_bias", "skip_nobias", "f16_params", "specials"])
+def test_register_layernorm_768(gpu_runtime, variant):
+    """Rows of 768 values, enough of them (2400) for the warp-per-row path,
+    which holds them in registers."""
+    rng = np.random.default_rng(len(variant))
+    x = (rng.standard_normal((4, 600, 768)) * 2 + 0.5).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, 768).astype(np.float32)
+    beta = (rng.standard_normal(768) * 0.1).astype(np.float32) if variant != "plain" else None
+    skip = bias = None
+    eps = 1e-12 if variant.startswith("skip") else 1e-5
+    if variant.startswith("skip"):
+        skip = rng.standard_normal(x.shape).astype(np.float32)
+        bias = (rng.standard_normal(768) * 0.1).astype(np.float32) if variant == "skip_bias" else None
+    if variant == "f16_params":
+        gamma, beta = gamma.astype(np.float16), beta.astype(np.float16)
+    if variant == "specials":
+        x[0, 0, 3] = np.nan
+        x[0, 1, :] = 7.0                 # zero variance: (x - mu) / sqrt(eps)
+        x[1, 2, 5] = np.inf
+        x[2, 3, 100] = 1e30
+    want = _oracle_ln(x, skip, bias, gamma, beta, eps)
+    d = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()   # noqa: E731
+    got = gpu_runtime.layernorm(d(x), d(skip), d(bias), d(gamma), d(beta), -1, eps)
+    assert_same(got.cpu().numpy(), want, f"layernorm 768 {variant}")
