@@ -64,6 +64,7 @@ _UNARY_NP = {"Sqrt": np.sqrt, "Exp": np.exp, "Sin": np.sin, "Cos": np.cos, "Atan
              "Tanh": np.tanh, "Sigmoid": lambda v: 1.0 / (1.0 + np.exp(-v)), "Floor": np.floor,
              "Round": np.rint, "Erf": None}
 COMPARE = {"Greater": "GREATER", "Less": "LESS", "GreaterOrEqual": "GEQ"}
+_BINARY = {"Add": "ADD", "Sub": "SUB", "Mul": "MUL", "Div": "DIV", "Pow": "POW"}
 _F16_TWO = np.array(2.0, dtype=np.float16)   # the Snake exponent constant of the graph
 
 
@@ -76,13 +77,27 @@ def as_cuda_device(device):
     return torch.device("cuda", int(device))
 
 
+_NP_OF_TORCH = {k: np.dtype(v) for k, v in TORCH_TO_NP.items()}
+
+
 def np_dtype(t):
-    return np.dtype(TORCH_TO_NP[t.dtype])
+    return _NP_OF_TORCH[t.dtype]
+
+
+_F16 = np.dtype(np.float16)
+_F32 = np.dtype(np.float32)
 
 
 def _wide(dt):
     """fp16 is widened to fp32 before compute (ref_runtime.py:49-51)."""
-    return np.dtype(np.float32) if dt == np.float16 else np.dtype(dt)
+    return _F32 if dt == _F16 else np.dtype(dt)
+
+
+@functools.lru_cache(maxsize=4096)
+def _bshape(*shapes):
+    """numpy's broadcast shape of the given shapes (cached: the same node
+    shapes recur for every utterance)."""
+    return np.broadcast_shapes(*shapes)
 
 
 def _probe(dt):
@@ -145,6 +160,7 @@ class BtRuntime:
         with torch.cuda.device(self.device):
             check(self.lib.bt_init(self.device.index), "bt_init")
         self._consts = {}
+        self._ew_plans = {}
         self.launches = 0
 
     # ---- device values ---------------------------------------------------------
@@ -182,10 +198,37 @@ class BtRuntime:
         return torch.empty(tuple(int(s) for s in shape), dtype=NP_TO_TORCH[np.dtype(dt)], device=self.device)
 
     def _stream(self):
+        """Points the library at this thread's current CUDA stream (set on
+        every launch: other callers on the thread may have set another)."""
         check(self.lib.bt_set_stream(_raw_stream(self.device.index)), "bt_set_stream")
 
     # ---- kernels ------------------------------------------------------------------
     def elementwise(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
+        """One element-wise launch.  Everything but the data pointers depends
+        only on the inputs' dtypes, shapes and strides, so it is prepared once
+        per such signature (numpy's result layout, the descriptors, the
+        attribute block) and reused: a call then allocates the result, writes
+        the pointers into the prepared descriptors and launches."""
+        key = (opname, tuple(out_shape), out_dt, compute_dt, alpha,
+               tuple((t.dtype, t.shape, t.stride()) for t in inputs))
+        plan = self._ew_plans.get(key)
+        if plan is None:
+            plan = self._ew_prepare(opname, inputs, out_shape, out_dt, compute_dt, alpha)
+            if len(self._ew_plans) >= 8192:
+                self._ew_plans.clear()
+            self._ew_plans[key] = plan
+        alloc_shape, tdt, back, code, descs, od, attrs, numel = plan
+        out = torch.empty(alloc_shape, dtype=tdt, device=self.device)
+        if numel:
+            for i, t in enumerate(inputs):
+                descs[i].data = t.data_ptr()
+            od.data = out.data_ptr()
+            self._stream()
+            check(self.lib.bt_elementwise(code, len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
+            self.launches += 1
+        return out if back is None else out.permute(back)
+
+    def _ew_prepare(self, opname, inputs, out_shape, out_dt, compute_dt, alpha):
         out_shape = tuple(int(v) for v in out_shape)
         back = None
         if any(not t.is_contiguous() for t in inputs):
@@ -198,15 +241,16 @@ class BtRuntime:
                 inputs = [t.view((1,) * (nd - t.dim()) + tuple(t.shape)).permute(order) for t in inputs]
                 out_shape = tuple(out_shape[a] for a in order)
                 back = _inverse(order)
-        out = self._empty(out_shape, out_dt)
-        if out.numel() > 0:
-            descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
-            attrs = _ew_attrs(np.dtype(compute_dt), float(alpha))
-            od = tensor_desc(out)
-            self._stream()
-            check(self.lib.bt_elementwise(OP[opname], len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
-            self.launches += 1
-        return out if back is None else out.permute(back)
+        tdt = NP_TO_TORCH[np.dtype(out_dt)]
+        numel = int(np.prod(out_shape, dtype=np.int64)) if out_shape else 1
+        descs = (_lib.BtTensor * len(inputs))(*[tensor_desc(t) for t in inputs])
+        strides, acc = [], 1
+        for d in reversed(out_shape):
+            strides.append(acc)
+            acc *= d
+        od = make_tensor(0, np.dtype(out_dt), out_shape, tuple(reversed(strides)))
+        attrs = _ew_attrs(np.dtype(compute_dt), float(alpha))
+        return out_shape, tdt, back, OP[opname], descs, od, attrs, numel
 
     # ---- data movement: strided copies through the IDENTITY kernel ----------------
     @staticmethod
@@ -319,6 +363,21 @@ class BtRuntime:
 
     # ---- the op table -----------------------------------------------------------------
     def dispatch(self, op, node_input, node_output, at, env):
+        if op in _BINARY:
+            # the most frequent nodes, without the helpers below
+            x, y = env[node_input[0]], env[node_input[1]]
+            if not isinstance(x, torch.Tensor) or not x.is_cuda:
+                x = self.to_device(x)
+            if not isinstance(y, torch.Tensor) or not y.is_cuda:
+                y = self.to_device(y)
+            a, b = _wide(_NP_OF_TORCH[x.dtype]), _wide(_NP_OF_TORCH[y.dtype])
+            dt = _binary_result(op, a, b)
+            if op == "Pow" and dt.kind != "f":
+                raise NotImplementedError("integer Pow is not on the GPU path")
+            env[node_output[0]] = self.elementwise(_BINARY[op], [x, y], _bshape(tuple(x.shape), tuple(y.shape)),
+                                                   dt, self._compute(dt))
+            return
+
         def arg(i, default=None):
             if i >= len(node_input) or not node_input[i]:
                 return default
@@ -331,7 +390,7 @@ class BtRuntime:
         if op in ("Add", "Sub", "Mul", "Div", "Pow"):
             x, y = dev(0), dev(1)
             a, b = _wide(np_dtype(x)), _wide(np_dtype(y))
-            shape = np.broadcast_shapes(tuple(x.shape), tuple(y.shape))
+            shape = _bshape(tuple(x.shape), tuple(y.shape))
             dt = _binary_result(op, a, b)
             if op == "Pow" and dt.kind != "f":
                 raise NotImplementedError("integer Pow is not on the GPU path")
@@ -530,6 +589,7 @@ class BtRuntime:
 
     # ---- helpers --------------------------------------------------------------------------
     @staticmethod
+    @functools.lru_cache(maxsize=64)
     def _compute(dt):
         dt = np.dtype(dt)
         if dt == np.float16:
