@@ -12,6 +12,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
 }
+// 8-byte copy; both addresses 8-byte aligned.
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem_src) : "memory");
+}
 // 4-byte copy; both addresses 4-byte aligned.
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);

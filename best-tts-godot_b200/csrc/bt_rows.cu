@@ -1051,15 +1051,30 @@ __global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
     mk[k] = make_float2(0.0f, 0.0f);
     if (mconst && e < N) mk[k] = make_float2(a.mask[e * a.mask_col_st], a.mask[(e + 1) * a.mask_col_st]);
   }
-  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
-       row += (int64_t)gridDim.x * kWarpsPerCta) {
-    const float* xr = a.x + row * N;
+  // The next row of this warp is copied into shared memory (cp.async, each
+  // lane its own pairs) while the current one is computed: two buffers per
+  // warp, [buffer][slot][lane].
+  __shared__ __align__(16) float2 stage[kWarpsPerCta][2][8][32];
+  const int w = threadIdx.x >> 5;
+  const int64_t step = (int64_t)gridDim.x * kWarpsPerCta;
+  auto prefetch = [&](int64_t r, int buf) {
+    const float* xr = a.x + r * N;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (e0 + 8 * k < N) cp_async8(&stage[w][buf][k][lane], xr + e0 + 8 * k);
+    cp_async_commit();
+  };
+  int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + w;
+  if (row < a.rows) prefetch(row, 0);
+  for (int it = 0; row < a.rows; row += step, ++it) {
+    const int buf = it & 1;
+    if (row + step < a.rows) prefetch(row + step, buf ^ 1);
+    else cp_async_commit();              // an empty group keeps the count
+    cp_async_wait<1>();                  // this row's copies (this lane's own)
     float2 v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int e = e0 + 8 * k;
-      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
-    }
+    for (int k = 0; k < 8; ++k)
+      v[k] = e0 + 8 * k < N ? stage[w][buf][k][lane] : make_float2(-INFINITY, -INFINITY);
     if (a.mask) {
       if (mconst) {
 #pragma unroll
@@ -1113,22 +1128,51 @@ __global__ void __launch_bounds__(256) wrow_softmax_reg_kernel(SoftmaxArgs a) {
 // (Skip +) layer norm over rows of N values held in registers (see the
 // register-resident rows above): numpy's mean, then the mean of the squared
 // deviations, each a pairwise sum unrolled at compile time; the output steps
-// Sub -> Div -> Mul(gamma) [-> Add(beta)], each rounded.
+// Sub -> Div -> Mul(gamma) [-> Add(beta)], each rounded.  CTAs of four
+// warps; each warp copies its next row into shared memory (cp.async) while
+// it computes the current one, and gamma, beta and the skip bias sit in
+// shared memory in the lanes' own order (float32, read once per CTA).
+constexpr int kLnWarps = 4;
 template <int N>
-__global__ void __launch_bounds__(256) wrow_layernorm_reg_kernel(LayerNormArgs a) {
+__global__ void __launch_bounds__(32 * kLnWarps) wrow_layernorm_reg_kernel(LayerNormArgs a) {
   constexpr int NS = reg_slots<N>();
   static_assert(N % 8 == 0 && NS <= 12, "rows of a multiple of 8 values, at most 768");
-  const int lane = threadIdx.x & 31;
+  __shared__ __align__(16) float2 stage[kLnWarps][2][NS][32];
+  __shared__ __align__(16) float2 sg[NS][32], sb[NS][32], sbias[NS][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int e0 = 8 * NS * (lane >> 2) + 2 * (lane & 3);   // element of slot 0
-  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
-       row += (int64_t)gridDim.x * kWarpsPerCta) {
-    const float* xr = a.x + row * N;
+  for (int i = threadIdx.x; i < NS * 32; i += 32 * kLnWarps) {
+    const int k = i >> 5, l = i & 31;
+    const int e = 8 * NS * (l >> 2) + 2 * (l & 3) + 8 * k;
+    float2 g = make_float2(0.0f, 0.0f), be = g, bi = g;
+    if (e < N) {
+      g = make_float2(ldf(a.gamma, a.gdt, e), ldf(a.gamma, a.gdt, e + 1));
+      if (a.beta) be = make_float2(ldf(a.beta, a.bdt, e), ldf(a.beta, a.bdt, e + 1));
+      if (a.bias) bi = make_float2(a.bias[e], a.bias[e + 1]);
+    }
+    sg[k][l] = g;
+    sb[k][l] = be;
+    sbias[k][l] = bi;
+  }
+  __syncthreads();
+  const int64_t step = (int64_t)gridDim.x * kLnWarps;
+  auto prefetch = [&](int64_t r, int buf) {
+    const float* xr = a.x + r * N;
+#pragma unroll
+    for (int k = 0; k < NS; ++k)
+      if (e0 + 8 * k < N) cp_async8(&stage[w][buf][k][lane], xr + e0 + 8 * k);
+    cp_async_commit();
+  };
+  int64_t row = (int64_t)blockIdx.x * kLnWarps + w;
+  if (row < a.rows) prefetch(row, 0);
+  for (int it = 0; row < a.rows; row += step, ++it) {
+    const int buf = it & 1;
+    if (row + step < a.rows) prefetch(row + step, buf ^ 1);
+    else cp_async_commit();              // an empty group keeps the count
+    cp_async_wait<1>();                  // this row's copies (this lane's own)
     float2 v[NS];
 #pragma unroll
-    for (int k = 0; k < NS; ++k) {
-      const int e = e0 + 8 * k;
-      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(0.0f, 0.0f);
-    }
+    for (int k = 0; k < NS; ++k) v[k] = e0 + 8 * k < N ? stage[w][buf][k][lane] : make_float2(0.0f, 0.0f);
     if (a.skip || a.bias) {
       const float* sk = a.skip ? a.skip + row * N : nullptr;
 #pragma unroll
@@ -1136,10 +1180,10 @@ __global__ void __launch_bounds__(256) wrow_layernorm_reg_kernel(LayerNormArgs a
         const int e = e0 + 8 * k;
         if (e < N) {
           if (sk) {
-            const float2 w = __ldcs(reinterpret_cast<const float2*>(sk + e));
-            v[k] = make_float2(BT_ADD(v[k].x, w.x), BT_ADD(v[k].y, w.y));
+            const float2 q = __ldcs(reinterpret_cast<const float2*>(sk + e));
+            v[k] = make_float2(BT_ADD(v[k].x, q.x), BT_ADD(v[k].y, q.y));
           }
-          if (a.bias) v[k] = make_float2(BT_ADD(v[k].x, a.bias[e]), BT_ADD(v[k].y, a.bias[e + 1]));
+          if (a.bias) v[k] = make_float2(BT_ADD(v[k].x, sbias[k][lane].x), BT_ADD(v[k].y, sbias[k][lane].y));
         }
       }
     }
@@ -1154,12 +1198,13 @@ __global__ void __launch_bounds__(256) wrow_layernorm_reg_kernel(LayerNormArgs a
     for (int k = 0; k < NS; ++k) {
       const int e = e0 + 8 * k;
       if (e < N) {
-        const float g0 = ldf(a.gamma, a.gdt, e), g1 = ldf(a.gamma, a.gdt, e + 1);
-        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), g0);
-        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), g1);
+        const float2 g = sg[k][lane];
+        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), g.x);
+        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), g.y);
         if (a.beta) {
-          y0 = BT_ADD(y0, ldf(a.beta, a.bdt, e));
-          y1 = BT_ADD(y1, ldf(a.beta, a.bdt, e + 1));
+          const float2 be = sb[k][lane];
+          y0 = BT_ADD(y0, be.x);
+          y1 = BT_ADD(y1, be.y);
         }
         __stcs(reinterpret_cast<float2*>(orow + e), make_float2(y0, y1));
       }
@@ -1790,9 +1835,9 @@ extern "C" int bt_layernorm(const bt_tensor* x, const bt_tensor* skip, const bt_
           (!a.skip || ((uintptr_t)a.skip & 7) == 0)) {
         DevInfo di;
         const int sms = (dev_info(&di) == BT_OK && di.sm_count > 0) ? di.sm_count : 148;
-        const int64_t need = (rows + kWarpsPerCta - 1) / kWarpsPerCta;
-        const int64_t cap = (int64_t)sms * 8;
-        wrow_layernorm_reg_kernel<768><<<(int)(need < cap ? need : cap), 32 * kWarpsPerCta, 0, cur_stream()>>>(a);
+        const int64_t need = (rows + kLnWarps - 1) / kLnWarps;
+        const int64_t cap = (int64_t)sms * 6;   // six CTAs of four warps per SM (shared memory)
+        wrow_layernorm_reg_kernel<768><<<(int)(need < cap ? need : cap), 32 * kLnWarps, 0, cur_stream()>>>(a);
         return check_launch("bt_layernorm(register rows)");
       }
       WLayerNormArgs w{wp, a};
