@@ -4,14 +4,17 @@
 numpy op table for every node and once with HybridRuntime in its place
 (hot-path ops on the B200, every other op on the same numpy table).
 
-Two runs through the GPU table:
-  - every hot-path op whose kernels are bit-exact against numpy on the GPU,
-    the four ops whose numpy results come from libm / vendor routines
-    (Tanh, Atan, Erf inside FastGelu's tanh, FastGelu) on the CPU table: the
-    waveform must be identical bit for bit;
-  - every hot-path op on the GPU: those four ops are within 2 ulp of numpy,
-    so the waveform may differ in its last bits; it must stay within
-    1e-4 of the reference's peak amplitude.
+  - Every hot-path op whose kernels are bit-exact against numpy on the GPU,
+    the ops whose numpy results come from numpy's own vector tanh and
+    arctan (Tanh, Atan, FastGelu, and Erf) on the CPU table: the waveform
+    must be identical bit for bit.
+  - Every hot-path op on the GPU.  The GPU's tanh and arctan are correctly
+    rounded (within 1 ulp of numpy's), and this model's waveform moves by
+    up to 0.06 (of a 0.38 peak) under 1-ulp changes of FastGelu's tanh --
+    the reference itself does the same with a correctly rounded tanh (its
+    prosody path rounds durations).  So the comparison is against the
+    reference's own op table with those three ops' tanh / arctan taken in
+    float64 and rounded to float32, everything else unchanged.
 
 This needs the reference's model and CPU ops, which are not part of this
 repository: set BT_REFERENCE_CHECKOUT to a best-tts-godot checkout (it reads
@@ -93,12 +96,53 @@ def test_waveform_bit_identical_with_exact_ops_on_the_gpu(reference):
     assert not bad.any(), f"{int(bad.sum())} of {bad.size} samples differ, max |err| {np.abs(got - want).max()}"
 
 
-def test_waveform_close_with_every_hot_op_on_the_gpu(reference):
+def _cr(fn, v):
+    """fn of a float32 array evaluated in float64, rounded to float32."""
+    return fn(np.asarray(v, dtype=np.float64)).astype(np.float32)
+
+
+def _reference_cr_run(reference):
+    """The reference's own op table, with FastGelu's tanh, Tanh and Atan
+    correctly rounded (the expressions of ref_runtime.py:288-293, :466-469
+    otherwise unchanged)."""
+    ref_runtime, pm, ids, style, _ = reference
+    orig = ref_runtime.RefRuntime.dispatch
+    f32 = ref_runtime._f32
+
+    def cr(self, op, ins, outs, at, env):
+        if op not in ("FastGelu", "Tanh", "Atan"):
+            return orig(self, op, ins, outs, at, env)
+        x = f32(env[ins[0]])
+        if op == "Tanh":
+            env[outs[0]] = _cr(np.tanh, x)
+        elif op == "Atan":
+            env[outs[0]] = _cr(np.arctan, x)
+        else:
+            x = x.astype(np.float32)
+            if len(ins) > 1 and ins[1]:
+                x = x + f32(env[ins[1]]).astype(np.float32)
+            c = np.float32(0.7978845608028654)
+            env[outs[0]] = 0.5 * x * (1.0 + _cr(np.tanh, c * (x + 0.044715 * x * x * x)))
+
+    ref_runtime.RefRuntime.dispatch = cr
+    try:
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            return np.asarray(pm.run(ids, style))
+    finally:
+        ref_runtime.RefRuntime.dispatch = orig
+
+
+def test_waveform_with_every_hot_op_on_the_gpu(reference):
     from bt_b200.runtime import BtRuntime
-    want = reference[-1]
+    want = _reference_cr_run(reference)
+    numpy_run = reference[-1]
     got, stats = _hybrid_run(reference, set(BtRuntime.HOT_OPS))
     assert stats["gpu_nodes"] == 3442
+    assert got.dtype == want.dtype and got.shape == want.shape
     err = float(np.abs(got.astype(np.float64) - want).max())
     peak = float(np.abs(want).max())
-    print(f"waveform: {want.size} samples, max |err| {err:.3e}, peak {peak:.3e}")
-    assert err <= 1e-4 * peak
+    moved = float(np.abs(want.astype(np.float64) - numpy_run).max())
+    print(f"waveform: {want.size} samples, max |err| vs the correctly rounded reference {err:.3e}, "
+          f"peak {peak:.3e}; the reference moves by {moved:.3e} itself under correctly rounded tanh / arctan")
+    assert err <= 1e-6 * peak
