@@ -29,10 +29,12 @@
 // at run time.
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <type_traits>
 #include "bt_ops.h"
 #include "bt_internal.h"
 #include "bt_core.h"
 #include "bt_ewmath.h"
+#include "bt_pk.h"
 
 namespace bt {
 namespace {
@@ -193,14 +195,21 @@ constexpr uint32_t sig(uint32_t k0, uint32_t k1 = 0, uint32_t k2 = 0, uint32_t k
 }
 template <uint32_t SIG, int K>
 __host__ __device__ constexpr uint32_t kind_of() { return (SIG >> (4 * K)) & 15u; }
+// Snake over a float32 row with per-row alpha, exponent and inv_alpha
+constexpr uint32_t kSnakeSig = sig(kF32, kRow, kRow, kRow);
+// vectors in flight per thread: eight where a varying input is 8-bit (four
+// bytes per vector, so little is in flight otherwise), else two
+template <uint32_t SIG>
+__host__ __device__ constexpr int chain_unroll() {
+  return (kind_of<SIG, 0>() == kI8 || kind_of<SIG, 0>() == kU8) ? 8 : 2;
+}
 
 // Input K's VEC values of vector v (row offset off, row constant rowv).
 template <uint32_t SIG, int K, int VEC>
 __device__ __forceinline__ void load_in(const ChainIn& o, int64_t off, int64_t v, float rowv, float* x) {
   constexpr uint32_t kd = kind_of<SIG, K>();
   if constexpr (kd == kRow) {
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) x[j] = rowv;
+    // read from rowv where it is used (see lane_value)
   } else if constexpr (kd == kF32 && VEC == 4) {
     const float4 f = __ldcs((const float4*)((const float*)o.p + off + v * 4));
     x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
@@ -209,14 +218,9 @@ __device__ __forceinline__ void load_in(const ChainIn& o, int64_t off, int64_t v
     const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
     const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
     x[0] = f0.x; x[1] = f0.y; x[2] = f1.x; x[3] = f1.y;
-  } else if constexpr (kd == kI8 && VEC == 4) {
-    const int w = __ldcs((const int*)((const signed char*)o.p + off + v * 4));
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = (float)(signed char)(w >> (8 * j));
-  } else if constexpr (kd == kU8 && VEC == 4) {
-    const unsigned w = __ldcs((const unsigned*)((const unsigned char*)o.p + off + v * 4));
-#pragma unroll
-    for (int j = 0; j < 4; ++j) x[j] = (float)((w >> (8 * j)) & 0xffu);
+  } else if constexpr ((kd == kI8 || kd == kU8) && VEC == 4) {
+    // the four bytes stay packed in one register until they are used
+    x[0] = __int_as_float(__ldcs((const int*)((const signed char*)o.p + off + v * 4)));
   } else {
     if (o.inner == 0) {
 #pragma unroll
@@ -227,6 +231,16 @@ __device__ __forceinline__ void load_in(const ChainIn& o, int64_t off, int64_t v
       x[0] = ld1<float>(o.p, o.dt, off + v * o.inner);
     }
   }
+}
+
+// Value j of input k's vector (as load_in left it).
+template <uint32_t SIG, int VEC>
+__device__ __forceinline__ float lane_value(int k, int j, const float* xk, const float* rowv) {
+  const uint32_t kd = (SIG >> (4 * k)) & 15u;   // folds: k and j are unrolled constants
+  if (kd == kRow) return rowv[k];
+  if (VEC == 4 && kd == kI8) return (float)(signed char)(__float_as_int(xk[0]) >> (8 * j));
+  if (VEC == 4 && kd == kU8) return (float)((__float_as_uint(xk[0]) >> (8 * j)) & 0xffu);
+  return xk[j];
 }
 
 template <uint32_t SIG, int VEC, int K, int NIN>
@@ -242,6 +256,21 @@ struct LoadAll<SIG, VEC, NIN, NIN> {
   static __device__ __forceinline__ void run(const ChainLaunch&, const int64_t*, int64_t, const float*,
                                              float (*)[VEC]) {}
 };
+
+// Snake of four values two at a time (bt_pk.h), for rows whose exponent is
+// 2: alpha * x, numpy's sine squared as Pow(., 2) squares it, times
+// inv_alpha, added to x lane by lane (a packed product feeding a packed add
+// may be contracted into one FMA, which would round once instead of twice).
+__device__ __forceinline__ void snake4(const float (&x)[4], float al, float ial, float* out) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float2 v = make_float2(x[2 * h], x[2 * h + 1]);
+    const float2 s2 = pk_np_sin<true>(pk_mul(pk(al), v));
+    const float2 z = pk_add_lanes(v, pk_mul(pk(ial), s2));
+    out[2 * h] = z.x;
+    out[2 * h + 1] = z.y;
+  }
+}
 
 // U vectors of VEC values per thread in flight; every load of a vector is
 // issued before any of its math.
@@ -270,12 +299,20 @@ __global__ void __launch_bounds__(kChainThreads, SIG == 0 ? 1 : 4) chain_prog_ke
         const int64_t v = v0 + u * stride;
         if (v >= nv) break;
         float res[VEC];
+        auto each = [&]() {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          float reg[P::NREG];
+          for (int j = 0; j < VEC; ++j) {
+            float reg[P::NREG];
 #pragma unroll
-          for (int k = 0; k < NIN; ++k) reg[k] = x[u][k][j];
-          res[j] = P::eval(reg, a);
+            for (int k = 0; k < NIN; ++k) reg[k] = lane_value<SIG, VEC>(k, j, x[u][k], rowv);
+            res[j] = P::eval(reg, a);
+          }
+        };
+        if constexpr (std::is_same<P, ProgSnake>::value && SIG == kSnakeSig && VEC == 4) {
+          if (rowv[2] == 2.0f) snake4(x[u][0], rowv[1], rowv[3], res);
+          else each();
+        } else {
+          each();
         }
         if constexpr (VEC == 4) {
           __stcs((float4*)(orow + v * VEC), make_float4(res[0], res[1], res[2], res[3]));
@@ -429,7 +466,8 @@ int launch_prog(const ChainLaunch& a, bool vec, uint32_t actual, int sms, cudaSt
   bool done = false;
   if (vec)
     ((!done && actual == SIGS
-          ? (chain_prog_kernel<P, 4, U, SIGS><<<chain_grid(a, 4 * U * kChainThreads, sms), kChainThreads, 0, s>>>(a),
+          ? (chain_prog_kernel<P, 4, chain_unroll<SIGS>(), SIGS>
+             <<<chain_grid(a, 4 * chain_unroll<SIGS>() * kChainThreads, sms), kChainThreads, 0, s>>>(a),
              done = true)
           : false),
      ...);

@@ -124,8 +124,15 @@ __device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_
 // k lies in [-124, 124] and P5/Q2 in [0.7, 1.5], so pq * 2^k is normal and
 // exact -- numpy's two scaling multiplies round nothing -- and it is formed
 // by adding k << 23 to the bits of pq.
+// A lane at or below numpy's underflow bound (-103.972..., where np_expf
+// returns +0: masked softmax keys, large sigmoid arguments) stays on this
+// path too, computing on 0 and selecting +0 at the end, so a warp whose rows
+// hold such values does not split between the two paths.
 __device__ __forceinline__ float2 pk_np_exp(float2 x) {
-  if (!(fabsf(x.x) < 86.0f && fabsf(x.y) < 86.0f)) return pk_exp_edge(x);
+  const float kXmin = -103.97208404541015625f;
+  const bool ux = x.x <= kXmin, uy = x.y <= kXmin;
+  if (!((fabsf(x.x) < 86.0f || ux) && (fabsf(x.y) < 86.0f || uy))) return pk_exp_edge(x);
+  x = make_float2(ux ? 0.0f : x.x, uy ? 0.0f : x.y);
   const float kMagic = 12582912.0f;   // 1.5 * 2^23
   // product then sum: lane by lane (two roundings, see pk_add_lanes)
   const float2 t = pk_add_lanes(pk_mul(x, pk(1.442695040888963407359924681001892137f)), pk(kMagic));
@@ -140,8 +147,8 @@ __device__ __forceinline__ float2 pk_np_exp(float2 x) {
   float2 den = pk_fma(pk(2.159509375685829852307e-02f), r, pk(-2.742335390411667452936e-01f));
   den = pk_fma(den, r, pk(1.0f));
   const float2 pq = pk_div_nr(num, den);
-  return make_float2(__uint_as_float(__float_as_uint(pq.x) + (__float_as_uint(t.x) << 23)),
-                     __uint_as_float(__float_as_uint(pq.y) + (__float_as_uint(t.y) << 23)));
+  return make_float2(ux ? 0.0f : __uint_as_float(__float_as_uint(pq.x) + (__float_as_uint(t.x) << 23)),
+                     uy ? 0.0f : __uint_as_float(__float_as_uint(pq.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // 1 / (1 + exp(-x)) of both lanes, np_sigmoidf step for step: the quotient
