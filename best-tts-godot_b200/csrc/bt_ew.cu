@@ -397,6 +397,9 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
 #pragma unroll
     for (int k = 0; k < NIN; ++k)
       if (a.in[k].st[1] == 0) rowv[k] = ld1<float>(a.in[k].p, a.in[k].dt, r * a.in[k].st[0]);
+    // Div by a divisor constant along the row: its double reciprocal, once
+    const bool row_div = OP == BT_OP_DIV && a.in[NIN - 1].st[1] == 0;
+    const double rdiv = row_div ? recip_d(rowv[NIN - 1]) : 0.0;
     for (int64_t v0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v0 < nv; v0 += U * stride) {
       float x[U][NIN][VEC];
 #pragma unroll
@@ -424,7 +427,17 @@ __global__ void __launch_bounds__(256) ew_rows_op_kernel(EwArgs a) {
         const int64_t t = (v0 + u * stride) * VEC;
         if (v0 + u * stride >= nv) break;
         float res[VEC];
-        if constexpr (VEC == 4 && OP >= 0) {
+        if constexpr (OP == BT_OP_DIV) {
+          if (row_div) {
+            // the row's divisor is one float: RN32(RN64(x * r)) with r within
+            // a double ulp of 1 / b is RN32(x / b) for every float x, b
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) res[j] = div_by(x[u][0][j], rdiv);
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) res[j] = BT_DIV(x[u][0][j], x[u][1][j]);
+          }
+        } else if constexpr (VEC == 4 && OP >= 0) {
           const float4 v4 = apply_vec4<OP>(a, f4(x[u][0]), NIN > 1 ? f4(x[u][NIN - 1]) : make_float4(0.f, 0.f, 0.f, 0.f),
                                            make_float4(0.f, 0.f, 0.f, 0.f));
           res[0] = v4.x; res[1] = v4.y; res[2] = v4.z; res[3] = v4.w;
