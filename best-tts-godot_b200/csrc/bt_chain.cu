@@ -198,10 +198,11 @@ __host__ __device__ constexpr uint32_t kind_of() { return (SIG >> (4 * K)) & 15u
 // Snake over a float32 row with per-row alpha, exponent and inv_alpha
 constexpr uint32_t kSnakeSig = sig(kF32, kRow, kRow, kRow);
 // vectors in flight per thread: eight where a varying input is 8-bit (four
-// bytes per vector, so little is in flight otherwise), else two
+// bytes per vector, so little is in flight otherwise), else four (two for
+// the layout-generic kernels, whose every input may vary)
 template <uint32_t SIG>
 __host__ __device__ constexpr int chain_unroll() {
-  return (kind_of<SIG, 0>() == kI8 || kind_of<SIG, 0>() == kU8) ? 8 : 2;
+  return SIG == 0 ? 2 : (kind_of<SIG, 0>() == kI8 || kind_of<SIG, 0>() == kU8) ? 8 : 4;
 }
 
 // Input K's VEC values of vector v (row offset off, row constant rowv).
@@ -275,7 +276,7 @@ __device__ __forceinline__ void snake4(const float (&x)[4], float al, float ial,
 // U vectors of VEC values per thread in flight; every load of a vector is
 // issued before any of its math.
 template <class P, int VEC, int U, uint32_t SIG>
-__global__ void __launch_bounds__(kChainThreads, SIG == 0 ? 1 : 4) chain_prog_kernel(ChainLaunch a) {
+__global__ void __launch_bounds__(kChainThreads, SIG == 0 ? 1 : (U == 4 ? 3 : 4)) chain_prog_kernel(ChainLaunch a) {
   constexpr int NIN = P::NIN;
   const int64_t R = a.R, T = a.T;
   const int64_t nv = T / VEC;
