@@ -376,10 +376,12 @@ __host__ __device__ constexpr int fixed_n_in() {
   return (OP == BT_OP_ADD || OP == BT_OP_SUB || OP == BT_OP_MUL || OP == BT_OP_DIV || OP == BT_OP_POW) ? 2 : 1;
 }
 // Vectors each thread of ew_rows_op_kernel loads before it computes (one
-// where a call to an out-of-line path would otherwise need a stack frame).
+// where a call to an out-of-line path would otherwise need a stack frame;
+// Div keeps four: by a row-constant divisor it multiplies by the divisor's
+// double reciprocal, and its per-element quotient fits the registers).
 template <int OP>
 __host__ __device__ constexpr int rows_unroll() {
-  return (OP == BT_OP_DIV || OP == BT_OP_SIGMOID || OP == BT_OP_GELU || OP == BT_OP_POW) ? 1 : 4;
+  return (OP == BT_OP_SIGMOID || OP == BT_OP_GELU || OP == BT_OP_POW) ? 1 : 4;
 }
 
 // The same with the op fixed at compile time (OP >= 0, VEC = 4): each thread
