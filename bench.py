@@ -380,6 +380,10 @@ def per_op(rt, torch, peak):
     ms, gbs = measure_op(lambda: rt.snake(A3s, al8, ial8, two16), 2 * n * 4 + 128 * 4, flush, 5, torch)
     sweep["snake_chain"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4),
                             "launches": 1}
+    from bt_b200 import chains
+    ms, gbs = measure_op(lambda: rt.chain(chains.add_unary_program("SIGMOID"), [A, A2]), 3 * n * 4, flush, 5, torch)
+    sweep["add_sigmoid_chain"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4),
+                                  "launches": 1}
     gl = torch.rand(768, device="cuda")
     Al = A.reshape(-1)[: (n // 768) * 768].reshape(-1, 768)
     Al2 = A2.reshape(-1)[: (n // 768) * 768].reshape(-1, 768)
