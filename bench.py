@@ -366,8 +366,7 @@ def per_op(rt, torch, peak):
     W8 = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda", generator=gq8)
     sc8 = torch.rand((8192, 1), device="cuda", generator=gq8) * 0.02 + 1e-3
     gn8 = torch.rand((8192, 1), device="cuda", generator=gq8) + 0.5
-    ms, gbs = measure_op(lambda: rt.elementwise("DEQUANT", [W8, sc8], W8.shape, np.float32, np.float32),
-                         n * 5 + 8192 * 4, flush, 5, torch)
+    ms, gbs = measure_op(lambda: rt.dequantize(W8, sc8), n * 5 + 8192 * 4, flush, 5, torch)
     sweep["dequant_int8"] = {"ms": round(ms, 4), "GBps": round(gbs, 1), "frac_of_measured": round(gbs / peak, 4)}
     ms, gbs = measure_op(lambda: rt.dequant_mul(W8, sc8, None, gn8), n * 5 + 8192 * 8, flush, 5, torch)
     sweep["dequant_int8_x_gain_chain"] = {"ms": round(ms, 4), "GBps": round(gbs, 1),

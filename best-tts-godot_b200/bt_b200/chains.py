@@ -41,12 +41,19 @@ def program(n_in, code, out_reg):
     return prog
 
 
-# The library's catalog (bt_chain_kind 0-5), inputs in the order listed.
+# The library's catalog (bt_chain_kind 0-7), inputs in the order listed.
 def dequant_mul_program(with_zp):
     """Mul(DequantizeLinear(q, scale[, zp]), gain): inputs q, scale, gain[, zp]."""
     if with_zp:
         return program(4, [("SUB", 4, 0, 3), ("MUL", 4, 4, 1), ("MUL", 4, 4, 2)], 4)
     return program(3, [("MUL", 3, 0, 1), ("MUL", 3, 3, 2)], 3)
+
+
+def dequant_program(with_zp):
+    """DequantizeLinear(q, scale[, zp]) = (q [- zp]) * scale: inputs q, scale[, zp]."""
+    if with_zp:
+        return program(3, [("SUB", 3, 0, 2), ("MUL", 3, 3, 1)], 3)
+    return program(2, [("MUL", 2, 0, 1)], 2)
 
 
 def snake_program():

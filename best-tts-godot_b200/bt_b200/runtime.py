@@ -464,9 +464,7 @@ class BtRuntime:
                 out = self.elementwise("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
         elif op == "DequantizeLinear":                          # ref :631-636
             q, scale, zp = dev(0), dev(1), dev(2)
-            ins = [q, scale] + ([zp] if zp is not None else [])
-            shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
-            out = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
+            out = self.dequantize(q, scale, zp)
         elif op == "DynamicQuantizeLinear":                     # ref :106-116, :625-630
             x = dev(0)
             if np_dtype(x) not in (np.float32, np.float16):
@@ -875,6 +873,19 @@ class BtRuntime:
         d = self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
         shape2 = np.broadcast_shapes(shape, tuple(gain.shape))
         return self.elementwise("MUL", [d, self._as_f32(gain)], shape2, np.float32, np.float32)
+
+    def dequantize(self, q, scale, zero_point=None):
+        """DequantizeLinear (ref_runtime.py:631-636): (q - zero_point) *
+        scale in float32.  8-bit q and zero point with a float32 / float16
+        scale run as one chain pass (bt_fused_chain, the 8-bit values read
+        packed); other dtypes on the element-wise DEQUANT op."""
+        from . import chains
+        ins = [q, scale] + ([zero_point] if zero_point is not None else [])
+        g = chains.FusedGroup(0, 0, "dequant", [], "", quant=(0, 2))
+        if g.inputs_ok([np_dtype(t) for t in ins]):
+            return self.chain(chains.dequant_program(zero_point is not None), ins)
+        shape = np.broadcast_shapes(*[tuple(t.shape) for t in ins])
+        return self.elementwise("DEQUANT", ins, shape, np.float32, np.float32)
 
     def snake(self, x, alpha, inv_alpha, power=None):
         """Snake x + inv_alpha * sin(alpha * x) ** power as the graph spells

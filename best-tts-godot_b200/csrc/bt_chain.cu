@@ -183,6 +183,10 @@ using ProgAddSigmoid = Prog<2, 3, In<BT_OP_ADD, 2, 0, 1, 0>, In<BT_OP_SIGMOID, 3
 using ProgMulAdd = Prog<3, 4, In<BT_OP_MUL, 3, 0, 1, 0>, In<BT_OP_ADD, 4, 3, 2, 1>>;
 // Add then LeakyRelu (a residual sum feeding an activation): inputs x, y
 using ProgAddLeaky = Prog<2, 3, In<BT_OP_ADD, 2, 0, 1, 0>, In<BT_OP_LEAKYRELU, 3, 2, 2, 1>>;
+// DequantizeLinear alone (ref_runtime.py:631-636): inputs q, scale
+using ProgDequant = Prog<2, 2, In<BT_OP_MUL, 2, 0, 1, 0>>;
+// DequantizeLinear with a zero point: inputs q, scale, zp
+using ProgDequantZp = Prog<3, 4, In<BT_OP_SUB, 3, 0, 2, 0>, In<BT_OP_MUL, 4, 3, 1, 1>>;
 
 // How a compiled kernel loads input k: SIG holds four bits per input.
 // kAny: decided at run time (row-constant or not, any dtype); kRow: the
@@ -447,7 +451,9 @@ int chain_canon(const bt_chain* prog, int (*canon)[4], int* out, const char* wha
   X(ProgSnake, sig(kF32, kRow, kRow, kRow))                                                          \
   X(ProgAddSigmoid, sig(kF32, kF32), sig(kF32, kRow))                                                \
   X(ProgMulAdd, sig(kF32, kRow, kRow), sig(kF32, kF32, kF32))                                        \
-  X(ProgAddLeaky, sig(kF32, kF32), sig(kF32, kRow))
+  X(ProgAddLeaky, sig(kF32, kF32), sig(kF32, kRow))                                                 \
+  X(ProgDequant, sig(kI8, kRow))                                                                     \
+  X(ProgDequantZp, sig(kI8, kRow, kRow))
 
 // Grid: rows in y, about 16 CTAs per SM in all, at least one per row.
 dim3 chain_grid(const ChainLaunch& a, int per_cta, int sms) {

@@ -166,6 +166,8 @@ int bt_fused_chain(const bt_chain* prog, const bt_tensor* in,
  *   3 Sigmoid(Add(x, y))                                inputs x, y
  *   4 Add(Mul(x, g), b)                                 inputs x, g, b
  *   5 LeakyRelu(Add(x, y))                              inputs x, y
+ *   6 DequantizeLinear(q, scale) (a Mul)                inputs q, scale
+ *   7 DequantizeLinear(q, scale, zp)                    inputs q, scale, zp
  * replaces: nothing in the reference (a query about this library's own
  *           kernels). */
 #define BT_CHAIN_INTERPRETER 64

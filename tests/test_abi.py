@@ -202,6 +202,8 @@ def test_chain_catalog_kinds(lib):
     assert kind(chains.add_unary_program("SIGMOID")) == 3
     assert kind(chains.mul_add_program()) == 4
     assert kind(chains.add_unary_program("LEAKYRELU", 0.1)) == 5
+    assert kind(chains.dequant_program(False)) == 6
+    assert kind(chains.dequant_program(True)) == 7
     # Snake written with fresh registers for every step: the same program
     fresh = chains.program(4, [("MUL", 4, 1, 0), ("SIN", 5, 4, 4), ("POW", 6, 5, 2), ("MUL", 7, 3, 6),
                                ("ADD", 8, 0, 7)], 8)

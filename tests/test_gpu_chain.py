@@ -227,7 +227,7 @@ def test_interpreter_random_programs_exact(rt, lib, seed):
     inputs.append(np.array(2.0, np.float32))
     prog, code, out = _random_program(rng, n_in, int(rng.integers(1, 10)), _EXACT)
     kind = lib.bt_chain_kind(ctypes.byref(prog))
-    assert kind == 64 or 0 <= kind < 6
+    assert kind == 64 or 0 <= kind < 8
     # numpy broadcasts inside each op, as the reference's graph does (a 0-d
     # exponent of 2 takes numpy's squaring path, which the kernels match)
     want = np.ascontiguousarray(np.broadcast_to(_run_np(code, n_in, [v.astype(np.float32) for v in inputs], out),
@@ -282,3 +282,35 @@ def test_run_nodes_fuses_known_chains(rt):
     inner = S.nodes[g0.nodes[0]][2][0]
     kept = rt.run_nodes(S.nodes, dict(denv), fuse=True, keep=keep | {inner})
     assert inner in kept
+
+
+@pytest.mark.parametrize("case", ["i8", "i8_zp", "u8_zp_f16scale", "per_tensor", "i32"])
+def test_dequantize_linear_alone(rt, case):
+    """DequantizeLinear through dispatch: 8-bit inputs take one chain pass,
+    int32 inputs the element-wise DEQUANT op; numpy's bits either way."""
+    rng = np.random.default_rng(11)
+    C = 64
+    q = rng.integers(-127, 128, (C, 48, 7)).astype(np.int8)
+    sc = rng.uniform(1e-3, 2e-2, (C, 1, 1)).astype(np.float32)
+    zp = None
+    if case == "i8_zp":
+        zp = rng.integers(-9, 10, (C, 1, 1)).astype(np.int8)
+    elif case == "u8_zp_f16scale":
+        q = rng.integers(0, 256, (C, 48, 7)).astype(np.uint8)
+        sc = sc.astype(np.float16)
+        zp = rng.integers(100, 156, (C, 1, 1)).astype(np.uint8)
+    elif case == "per_tensor":
+        sc = np.array(0.0123, np.float32)
+    elif case == "i32":
+        q = rng.integers(-10 ** 6, 10 ** 6, (C, 48, 7)).astype(np.int32)
+    env = {"q": q, "s": sc}
+    ins = ["q", "s"]
+    if zp is not None:
+        env["z"] = zp
+        ins.append("z")
+    want = oracle_nodes([("DequantizeLinear", ins, ["y"], {})], env, "y")
+    denv = {k: dev(v) for k, v in env.items()}
+    l0 = rt.launches
+    rt.dispatch("DequantizeLinear", ins, ["y"], {}, denv)
+    assert rt.launches - l0 == 1
+    assert_same(host(denv["y"]), want, f"DequantizeLinear {case}")
