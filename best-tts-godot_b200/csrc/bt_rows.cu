@@ -1024,9 +1024,38 @@ __device__ __forceinline__ float reg_leaf_sum(const float2 (&v)[NS], F f) {
   return res;
 }
 
+// Whether numpy's tree over a row of N values is eight leaves of one lane
+// group each (8 NS values, a multiple of 8, starting at group boundaries)
+// joined as ((L0+L1)+(L2+L3))+((L4+L5)+(L6+L7)): 768 values (12 slots) are.
+template <int NS, int N>
+__host__ __device__ constexpr bool group_tree() {
+  return N == 64 * NS && N / 8 <= kPwLeaf && N / 8 > 8 && pw_split_c(N) == N / 2 &&
+         pw_split_c(N / 2) == N / 4 && pw_split_c(N / 4) == N / 8;
+}
+
+// numpy's sum of f(values) over such a row: each group sums its leaf down
+// its slots and brackets it (two shuffles), then three xor shuffles across
+// groups join the leaves level by level, in every lane (each float sum
+// commutes, so the lanes of both partners get numpy's value).
+template <int NS, class F>
+__device__ __forceinline__ float reg_group_tree_sum(const float2 (&v)[NS], F f) {
+  float2 acc = f(v[0]);
+#pragma unroll
+  for (int k = 1; k < NS; ++k) {
+    const float2 t = f(v[k]);
+    acc = F::kPacked ? pk_add(acc, t) : make_float2(BT_ADD(acc.x, t.x), BT_ADD(acc.y, t.y));
+  }
+  float t = BT_ADD(acc.x, acc.y);
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) t = BT_ADD(t, __shfl_xor_sync(0xffffffffu, t, m));
+  return t;
+}
+
 template <int NS, int LEN, int OFF, class F>
 __device__ __forceinline__ float reg_pw_sum(const float2 (&v)[NS], F f) {
-  if constexpr (LEN <= kPwLeaf) {
+  if constexpr (OFF == 0 && group_tree<NS, LEN>()) {
+    return reg_group_tree_sum<NS>(v, f);
+  } else if constexpr (LEN <= kPwLeaf) {
     return reg_leaf_sum<NS, LEN, OFF>(v, f);
   } else {
     constexpr int S = pw_split_c(LEN);
@@ -1059,30 +1088,17 @@ __global__ void __launch_bounds__(256, 5) wrow_softmax_reg_kernel(SoftmaxArgs a)
     }
     __syncthreads();
   }
-  // The next row of this warp is copied into shared memory (cp.async, each
-  // lane its own pairs) while the current one is computed: two buffers per
-  // warp, [buffer][slot][lane].
-  __shared__ __align__(16) float2 stage[kWarpsPerCta][2][8][32];
-  const int w = threadIdx.x >> 5;
-  const int64_t step = (int64_t)gridDim.x * kWarpsPerCta;
-  auto prefetch = [&](int64_t r, int buf) {
-    const float* xr = a.x + r * N;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (e0 + 8 * k < N) cp_async8(&stage[w][buf][k][lane], xr + e0 + 8 * k);
-    cp_async_commit();
-  };
-  int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + w;
-  if (row < a.rows) prefetch(row, 0);
-  for (int it = 0; row < a.rows; row += step, ++it) {
-    const int buf = it & 1;
-    if (row + step < a.rows) prefetch(row + step, buf ^ 1);
-    else cp_async_commit();              // an empty group keeps the count
-    cp_async_wait<1>();                  // this row's copies (this lane's own)
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
+       row += (int64_t)gridDim.x * kWarpsPerCta) {
+    // the row straight into registers (each lane's eight pairs in flight at
+    // once; five CTAs of eight warps per SM keep enough rows in flight)
+    const float* xr = a.x + row * N;
     float2 v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      v[k] = e0 + 8 * k < N ? stage[w][buf][k][lane] : make_float2(-INFINITY, -INFINITY);
+    for (int k = 0; k < 8; ++k) {
+      const int e = e0 + 8 * k;
+      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
+    }
     if (a.mask) {
       if (mconst) {
 #pragma unroll
@@ -1148,7 +1164,8 @@ __global__ void __launch_bounds__(32 * kLnWarps, 8) wrow_layernorm_reg_kernel(La
   constexpr int NS = reg_slots<N>();
   static_assert(N % 8 == 0 && NS <= 12, "rows of a multiple of 8 values, at most 768");
   __shared__ __align__(16) float2 stage[kLnWarps][NS][32];
-  __shared__ __align__(16) float2 sg[NS][32], sb[NS][32], sbias[NS][32];
+  __shared__ __align__(16) float4 sgb[NS][32];   // (gamma pair, beta pair)
+  __shared__ __align__(16) float2 sbias[NS][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int e0 = 8 * NS * (lane >> 2) + 2 * (lane & 3);   // element of slot 0
   for (int i = threadIdx.x; i < NS * 32; i += 32 * kLnWarps) {
@@ -1160,8 +1177,7 @@ __global__ void __launch_bounds__(32 * kLnWarps, 8) wrow_layernorm_reg_kernel(La
       if (a.beta) be = make_float2(ldf(a.beta, a.bdt, e), ldf(a.beta, a.bdt, e + 1));
       if (a.bias) bi = make_float2(a.bias[e], a.bias[e + 1]);
     }
-    sg[k][l] = g;
-    sb[k][l] = be;
+    sgb[k][l] = make_float4(g.x, g.y, be.x, be.y);
     sbias[k][l] = bi;
   }
   __syncthreads();
@@ -1207,13 +1223,12 @@ __global__ void __launch_bounds__(32 * kLnWarps, 8) wrow_layernorm_reg_kernel(La
     for (int k = 0; k < NS; ++k) {
       const int e = e0 + 8 * k;
       if (e < N) {
-        const float2 g = sg[k][lane];
-        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), g.x);
-        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), g.y);
+        const float4 gb = sgb[k][lane];
+        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), gb.x);
+        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), gb.y);
         if (a.beta) {
-          const float2 be = sb[k][lane];
-          y0 = BT_ADD(y0, be.x);
-          y1 = BT_ADD(y1, be.y);
+          y0 = BT_ADD(y0, gb.z);
+          y1 = BT_ADD(y1, gb.w);
         }
         __stcs(reinterpret_cast<float2*>(orow + e), make_float2(y0, y1));
       }
