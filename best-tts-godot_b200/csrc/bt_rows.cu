@@ -1029,7 +1029,8 @@ __device__ __forceinline__ float reg_leaf_sum(const float2 (&v)[NS], F f) {
 // joined as ((L0+L1)+(L2+L3))+((L4+L5)+(L6+L7)): 768 values (12 slots) are.
 template <int NS, int N>
 __host__ __device__ constexpr bool group_tree() {
-  return N == 64 * NS && N / 8 <= kPwLeaf && N / 8 > 8 && pw_split_c(N) == N / 2 &&
+  // (every inner level must split: runs of at most kPwLeaf values are leaves)
+  return N == 64 * NS && N / 8 <= kPwLeaf && N / 8 > 8 && N / 4 > kPwLeaf && pw_split_c(N) == N / 2 &&
          pw_split_c(N / 2) == N / 4 && pw_split_c(N / 4) == N / 8;
 }
 
@@ -1037,6 +1038,9 @@ __host__ __device__ constexpr bool group_tree() {
 // its slots and brackets it (two shuffles), then three xor shuffles across
 // groups join the leaves level by level, in every lane (each float sum
 // commutes, so the lanes of both partners get numpy's value).
+static_assert(!group_tree<8, 512>(), "512 values: four 128-value leaves");
+static_assert(group_tree<12, 768>(), "768 values: eight 96-value leaves");
+
 template <int NS, class F>
 __device__ __forceinline__ float reg_group_tree_sum(const float2 (&v)[NS], F f) {
   float2 acc = f(v[0]);
