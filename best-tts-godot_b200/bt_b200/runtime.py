@@ -161,6 +161,7 @@ class BtRuntime:
             check(self.lib.bt_init(self.device.index), "bt_init")
         self._consts = {}
         self._ew_plans = {}
+        self._scalars = {}
         self.launches = 0
 
     # ---- device values ---------------------------------------------------------
@@ -585,6 +586,12 @@ class BtRuntime:
                 raise RuntimeError(f"{op} {list(outs)} failed: {exc}") from exc
         return env
 
+    def capture_nodes(self, nodes, env, warmup=1):
+        """The node list as one CUDA graph (see CapturedNodes): for a serving
+        loop that runs the same node sequence on inputs of the same shapes,
+        the per-node host work of ``dispatch`` is paid once, at capture."""
+        return CapturedNodes(self, nodes, env, warmup)
+
     # ---- helpers --------------------------------------------------------------------------
     @staticmethod
     @functools.lru_cache(maxsize=64)
@@ -623,7 +630,16 @@ class BtRuntime:
         else:
             info = np.iinfo(dt)
             v = info.min if low else info.max
-        return torch.tensor(np.array(v, dtype=dt)).to(self.device)
+        return self._scalar(v, dt)
+
+    def _scalar(self, value, dt):
+        """A 0-d device constant, uploaded once per (value, dtype): no host
+        copy inside a captured node list."""
+        key = (np.dtype(dt).str, np.array(value, dtype=dt).tobytes())
+        t = self._scalars.get(key)
+        if t is None:
+            t = self._scalars[key] = torch.tensor(np.array(value, dtype=dt)).to(self.device)
+        return t
 
     def dynamic_quantize(self, x, range=None):
         """DynamicQuantizeLinear of a float32 / float16 tensor
@@ -742,7 +758,7 @@ class BtRuntime:
     def _mean_from_sum(self, s, count):
         # np.mean divides the float32 sum by an intp count: float64 division,
         # rounded to float32.
-        c = torch.tensor(np.array(count, dtype=np.int64)).to(self.device)
+        c = self._scalar(count, np.int64)
         return self.elementwise("DIV", [s, c], s.shape, np.float32, np.float64)
 
     def softmax(self, x, mask, axis):
@@ -827,7 +843,7 @@ class BtRuntime:
         mu = self._reduce("ReduceMean", phys, paxes, {"keepdims": 1})
         d = self.elementwise("SUB", [phys, mu], phys.shape, f32, f32)
         var = self._reduce("ReduceMean", self.elementwise("MUL", [d, d], d.shape, f32, f32), paxes, {"keepdims": 1})
-        e = torch.tensor(np.float32(eps)).to(self.device)
+        e = self._scalar(np.float32(eps), np.float32)
         sd = self.elementwise("SQRT", [self.elementwise("ADD", [var, e], var.shape, f32, f32)], var.shape, f32, f32)
         y = self.elementwise("DIV", [d, sd], d.shape, f32, f32)
 
@@ -1038,3 +1054,34 @@ def _is_identity(perm):
 
 
 ctypes_i64 = ctypes.c_int64
+
+
+class CapturedNodes:
+    """A node list recorded once as a CUDA graph and replayed.
+
+    The list runs ``warmup`` times on a side stream first (numpy constants
+    are uploaded and per-stream scratch allocated there), then once more
+    under graph capture on the same stream.  ``env`` after capture holds the
+    graph's tensors: write new input values into them in place
+    (``cap.env[name].copy_(...)``) and ``replay()``; outputs are overwritten
+    in place on every replay.  Every node must keep its work on the device:
+    a node that needs a value on the host (a shape given as a CUDA tensor,
+    for instance) makes the capture fail."""
+
+    def __init__(self, rt, nodes, env, warmup=1):
+        self.rt = rt
+        self.stream = torch.cuda.Stream(rt.device)
+        self.stream.wait_stream(torch.cuda.current_stream(rt.device))
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                rt.run_nodes(nodes, dict(env))
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        self.env = dict(env)
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            rt.run_nodes(nodes, self.env)
+
+    def replay(self):
+        """Runs the recorded launches on the current stream; returns env."""
+        self.graph.replay()
+        return self.env
