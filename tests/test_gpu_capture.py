@@ -17,8 +17,11 @@ def test_captured_node_list_replays_exactly(gpu_runtime):
     rt = gpu_runtime
     S = build_stream(2, t0=8)
     host = C.c5_small_inputs(S, seed=5)
-    dev = {k: (torch.from_numpy(np.ascontiguousarray(v)).cuda() if isinstance(v, np.ndarray) and v.ndim > 0 else v)
-           for k, v in host.items()}
+    # activations on the device; the graph's constants (split sizes, axes,
+    # alpha) stay numpy arrays, as a model's initializers do
+    on_dev = lambda env: {k: (torch.from_numpy(np.ascontiguousarray(v)).cuda() if k in S.inputs else v)   # noqa: E731
+                          for k, v in env.items()}
+    dev = on_dev(host)
     cap = rt.capture_nodes(S.nodes, dev)
     out = cap.replay()
     torch.cuda.synchronize()
@@ -32,8 +35,6 @@ def test_captured_node_list_replays_exactly(gpu_runtime):
             cap.env[k].copy_(torch.from_numpy(np.ascontiguousarray(v)).reshape(cap.env[k].shape))
     out = cap.replay()
     torch.cuda.synchronize()
-    dev2 = {k: (torch.from_numpy(np.ascontiguousarray(v)).cuda() if isinstance(v, np.ndarray) and v.ndim > 0 else v)
-            for k, v in host2.items()}
-    eager2 = rt.run_nodes(S.nodes, dev2)
+    eager2 = rt.run_nodes(S.nodes, on_dev(host2))
     for name in S.stage_outputs():
         assert_same(out[name].cpu().numpy(), eager2[name].cpu().numpy(), f"replay 2 {name}")
