@@ -370,7 +370,9 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
         for (int i = threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
       }
     }
-    mu_w = div_by(BT_ADD(0.0f, tree_total(hs1, inner, A.P.D, true)), A.rT);
+    // (below 32 leaves only the first lanes of a warp hold the root: lane 0's)
+    const float sum = __shfl_sync(0xffffffffu, tree_total(hs1, inner, A.P.D, true), 0);
+    mu_w = div_by(BT_ADD(0.0f, sum), A.rT);
   } else if (threadIdx.x < 32) {
     const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   bool inr[BT_ADAIN_MAX_OUT] = {false, false, false};
   double rsd_w = 0.0;
   if (reg_tree) {
-    const float ssq = tree_total(hs2, inner, A.P.D, true);
+    const float ssq = __shfl_sync(0xffffffffu, tree_total(hs2, inner, A.P.D, true), 0);
     const float var = div_by(BT_ADD(0.0f, ssq), A.rT);
     const float sd = BT_SQRT(BT_ADD(var, A.eps));
     rsd_w = recip_d(sd);
