@@ -350,30 +350,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   int head = (4 - phase4(g0)) & 3;
   if (head > seg) head = seg;
   const int nvec = (seg - head) >> 2;
-  // A perfect tree of at most 512 leaves is summed in registers from the
-  // leaf sums alone (tree_total reads hs, writes nothing), so every warp
-  // sums it itself and no warp waits for another: the residual first, by
-  // all warps, then each warp's own total and row scalars.
-  // (not in the RANGE variants, whose range tracking leaves no registers
-  // for the per-warp row scalars)
-  const bool reg_tree = !RANGE && A.P.perfect != 0 && A.P.D <= 9;
-  float mu_w = 0.0f;
-  if (reg_tree) {
-    if (A.res) {
-      float* r = A.res + gofs;
-      if (phase4(r) == phase4(g0)) {
-        for (int q = threadIdx.x; q < nvec; q += kThreads)
-          __stcs((float4*)(r + head + 4 * q), *(const float4*)(b0 + head + 4 * q));
-        for (int i = threadIdx.x; i < head; i += kThreads) r[i] = b0[i];
-        for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
-      } else {
-        for (int i = threadIdx.x; i < seg; i += kThreads) r[i] = b0[i];
-      }
-    }
-    // (below 32 leaves only the first lanes of a warp hold the root: lane 0's)
-    const float sum = __shfl_sync(0xffffffffu, tree_total(hs1, inner, A.P.D, true), 0);
-    mu_w = div_by(BT_ADD(0.0f, sum), A.rT);
-  } else if (threadIdx.x < 32) {
+  if (threadIdx.x < 32) {
     const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
   } else if (A.res) {
@@ -390,29 +367,12 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
       for (int i = t; i < seg; i += kW) r[i] = b0[i];
     }
   }
-  if (!reg_tree) __syncthreads();
-  const float mu = reg_tree ? mu_w : s_mu;
+  __syncthreads();
+  const float mu = s_mu;
   // Sub, Mul(d, d), ReduceMean, Add eps, Sqrt
   slot_pass<1, true>(sw, ns, b0, nullptr, nullptr, mu, hs2, cluster, cs);
   sync_sums();
-  bool inr[BT_ADAIN_MAX_OUT] = {false, false, false};
-  double rsd_w = 0.0;
-  if (reg_tree) {
-    const float ssq = __shfl_sync(0xffffffffu, tree_total(hs2, inner, A.P.D, true), 0);
-    const float var = div_by(BT_ADD(0.0f, ssq), A.rT);
-    const float sd = BT_SQRT(BT_ADD(var, A.eps));
-    rsd_w = recip_d(sd);
-    if (SNAKE) {
-      // the bound of the single-warp path below, in every thread
-      const float nb = BT_MUL(BT_MUL(BT_SQRT(ssq), (float)rsd_w), 1.01f);
-#pragma unroll
-      for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) {
-        const float zb = BT_MUL(BT_MUL(fabsf(prm[k][2]), BT_ADD(BT_MUL(fabsf(prm[k][0]), nb), fabsf(prm[k][1]))),
-                                1.01f);
-        inr[k] = k < A.n_out && zb <= 0.5f * 117435.992f;
-      }
-    }
-  } else if (threadIdx.x < 32) {
+  if (threadIdx.x < 32) {
     const float ssq = tree_total(hs2, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) {
       const float var = div_by(BT_ADD(0.0f, ssq), A.rT);
@@ -435,12 +395,8 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
       }
     }
   }
-  if (!reg_tree) {
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < BT_ADAIN_MAX_OUT; ++k) inr[k] = in_range[k] != 0;
-  }
-  const double rsd = reg_tree ? rsd_w : s_rsd;
+  __syncthreads();
+  const double rsd = s_rsd;
 
   // the outputs of this segment (coalesced, 128-bit where the phases agree)
   const float2 nmu = pk(-mu);
@@ -494,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
     };
     float* o = A.out[k] + gofs;
     if (phase4(o) == phase4(g0)) {
-      if (SNAKE && inr[k]) vec_loop(o, std::false_type());
+      if (SNAKE && in_range[k]) vec_loop(o, std::false_type());
       else vec_loop(o, std::true_type());
       for (int i = threadIdx.x; i < head; i += kThreads) put(o, i);
       for (int i = head + 4 * nvec + threadIdx.x; i < seg; i += kThreads) put(o, i);
