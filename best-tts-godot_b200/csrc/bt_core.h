@@ -167,6 +167,50 @@ __device__ __forceinline__ float tanh_f(float x) {
 __device__ __forceinline__ float div_by(float a, double rb) {
   return __double2float_rn(__dmul_rn((double)a, rb));
 }
+
+// Division of many floats by one divisor b in float32 arithmetic alone
+// (Markstein's correction step with the correctly rounded reciprocal):
+//   y = RN(1/b) once, then per value  q0 = RN(a y),  r = RN(a - b q0) (an
+//   FMA),  q = RN(q0 + r y) (an FMA).
+// q == RN(a / b) whenever |a| and |b| lie in the window [2^-60, 2^60): then
+// a y, a / b, the residual and every step stay normal, so scaling a or b by
+// a power of two scales each step exactly, and the claim reduces to the
+// 2^46 pairs of significands in [1, 2) x [1, 2) -- which bt_selfcheck
+// (kind 7) checks one by one.  Values outside the window (zeros, subnormals,
+// infinities, NaN, huge or tiny values) and divisors outside it take div_by,
+// the double-precision path above; callers test the window with
+// div_row_outside and recompute those values.  Three float operations per
+// value instead of two conversions and a double product.
+struct RowDiv {
+  float b, y;       // the divisor and RN(1 / b)
+  uint32_t span;    // width of the window of |a|'s exponent field; 0 when b lies outside
+};
+constexpr uint32_t kRowDivLo = 67u << 23;      // 2^-60: biased exponent 67
+constexpr uint32_t kRowDivSpan = 120u << 23;   // up to 2^60 (biased exponent 186)
+__device__ __forceinline__ bool row_div_in_window(float v) {
+  return (f_bits(v) & 0x7f800000u) - kRowDivLo < kRowDivSpan;
+}
+__device__ __forceinline__ RowDiv row_div(float b) {
+  RowDiv d;
+  d.b = b;
+  d.y = __frcp_rn(b);
+  d.span = row_div_in_window(b) ? kRowDivSpan : 0u;
+  return d;
+}
+// the three-operation quotient, valid inside the window
+__device__ __forceinline__ float div_row_fast(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(-b, q0, a), y, q0);
+}
+// whether a lies outside the window (its quotient must come from div_by)
+__device__ __forceinline__ bool div_row_outside(float a, const RowDiv& d) {
+  return (f_bits(a) & 0x7f800000u) - kRowDivLo >= d.span;
+}
+// RN(a / b) for any a: the fast form inside the window, div_by with
+// rb = recip_d(b) outside (callers form rb only where some value needs it)
+__device__ __forceinline__ float div_row(float a, const RowDiv& d, double rb) {
+  return div_row_outside(a, d) ? div_by(a, rb) : div_row_fast(a, d.b, d.y);
+}
 #endif
 
 // ---------------------------------------------------------------------------

@@ -54,6 +54,14 @@ __device__ __forceinline__ float2 pk_fma(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// div_row_fast (bt_core.h) on two lanes that share the divisor b:
+// nb = (-b, -b), y2 = (RN(1/b), RN(1/b)).  Three packed operations for two
+// quotients; the window rules of div_row_fast apply lane by lane.
+__device__ __forceinline__ float2 pk_div_row_fast(float2 a, float2 nb, float2 y2) {
+  const float2 q0 = pk_mul(a, y2);
+  return pk_fma(pk_fma(nb, q0, a), y2, q0);
+}
+
 // Both lanes through the scalar function (arguments numpy does not reduce
 // itself, and NaN); out of line, it is almost never taken.
 template <bool COS, bool SQUARE>

@@ -1074,7 +1074,7 @@ template <int N>
 __host__ __device__ constexpr int reg_slots() { return ((N + 7) / 8 + 7) / 8; }
 
 template <int N>
-__global__ void __launch_bounds__(256, 5) wrow_softmax_reg_kernel(SoftmaxArgs a) {
+__global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a) {
   static_assert(N % 2 == 0 && N >= 2 && N <= 512, "rows of an even length up to 512");
   static_assert(reg_slots<N>() == 8, "eight slots per lane");
   const int lane = threadIdx.x & 31;
@@ -1092,17 +1092,25 @@ __global__ void __launch_bounds__(256, 5) wrow_softmax_reg_kernel(SoftmaxArgs a)
     }
     __syncthreads();
   }
-  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5); row < a.rows;
-       row += (int64_t)gridDim.x * kWarpsPerCta) {
-    // the row straight into registers (each lane's eight pairs in flight at
-    // once; five CTAs of eight warps per SM keep enough rows in flight)
-    const float* xr = a.x + row * N;
-    float2 v[8];
+  // rows straight into registers, the next row's loads issued before the
+  // current row is computed (each lane's eight pairs of both rows in flight)
+  const int64_t stride = (int64_t)gridDim.x * kWarpsPerCta;
+  int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+  float2 nx[8];
+  auto load_row = [&](int64_t r) {
+    const float* xr = a.x + r * N;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int e = e0 + 8 * k;
-      v[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
+      nx[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
     }
+  };
+  if (row < a.rows) load_row(row);
+  for (; row < a.rows; row += stride) {
+    float2 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = nx[k];
+    if (row + stride < a.rows) load_row(row + stride);
     if (a.mask) {
       if (mconst) {
 #pragma unroll
@@ -1143,12 +1151,32 @@ __global__ void __launch_bounds__(256, 5) wrow_softmax_reg_kernel(SoftmaxArgs a)
       if (e0 + 8 * k < N) v[k] = pk_np_exp(pk_add(v[k], nm));
     const float total = reg_pw_sum<8, N, 0>(v, RegIdentity());
     const float denom = BT_ADD(0.0f, total);
-    const double rd = recip_d(denom);
-    float* orow = a.out + row * N;
+    // The quotients in float32 (div_row_fast, two lanes at a time).  The
+    // denominator lies in [1, 512] (the row's maximum contributes exp(0) = 1)
+    // or is NaN, and every value in [0, 1] or NaN, so only values in
+    // (0, 2^-60) leave the window; +0 gives +0 exactly (0 y = 0, residual
+    // +0) and NaN stays NaN.  A lane holding such a value divides in double.
+    const float2 nb = pk(-denom), y2 = pk(__frcp_rn(denom));
+    bool tiny = false;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int e = e0 + 8 * k;
-      if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
+      tiny |= f_bits(v[k].x) - 1u < kRowDivLo - 1u;
+      tiny |= f_bits(v[k].y) - 1u < kRowDivLo - 1u;
+    }
+    float* orow = a.out + row * N;
+    if (!tiny) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = e0 + 8 * k;
+        if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), pk_div_row_fast(v[k], nb, y2));
+      }
+    } else {
+      const double rd = recip_d(denom);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = e0 + 8 * k;
+        if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
+      }
     }
   }
 }
@@ -1221,15 +1249,32 @@ __global__ void __launch_bounds__(32 * kLnWarps, 8) wrow_layernorm_reg_kernel(La
     const float ssq = reg_pw_sum<NS, N, 0>(v, RegSquaredDev{mu});
     const float var = np_mean_from_sum(BT_ADD(0.0f, ssq), N);
     const float sd = BT_SQRT(BT_ADD(var, a.eps));
-    const double rsd = recip_d(sd);
+    // (x - mu) / sd in float32 (div_row_fast, two lanes at a time); a lane
+    // holding a deviation outside the window divides all its values in double
+    const RowDiv dv = row_div(sd);
+    bool outside = false;
+#pragma unroll
+    for (int k = 0; k < NS; ++k) {
+      v[k] = make_float2(BT_SUB(v[k].x, mu), BT_SUB(v[k].y, mu));
+      if (e0 + 8 * k < N) outside |= div_row_outside(v[k].x, dv) | div_row_outside(v[k].y, dv);
+    }
+    if (!outside) {
+      const float2 nb = pk(-dv.b), y2 = pk(dv.y);
+#pragma unroll
+      for (int k = 0; k < NS; ++k) v[k] = pk_div_row_fast(v[k], nb, y2);
+    } else {
+      const double rb = recip_d(sd);   // div_by is exact for every value
+#pragma unroll
+      for (int k = 0; k < NS; ++k) v[k] = make_float2(div_by(v[k].x, rb), div_by(v[k].y, rb));
+    }
     float* orow = a.out + row * N;
 #pragma unroll
     for (int k = 0; k < NS; ++k) {
       const int e = e0 + 8 * k;
       if (e < N) {
         const float4 gb = sgb[k][lane];
-        float y0 = BT_MUL(div_by(BT_SUB(v[k].x, mu), rsd), gb.x);
-        float y1 = BT_MUL(div_by(BT_SUB(v[k].y, mu), rsd), gb.y);
+        float y0 = BT_MUL(v[k].x, gb.x);
+        float y1 = BT_MUL(v[k].y, gb.y);
         if (a.beta) {
           y0 = BT_ADD(y0, gb.z);
           y1 = BT_ADD(y1, gb.w);

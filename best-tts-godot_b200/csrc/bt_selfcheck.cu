@@ -1,7 +1,7 @@
 // bt_selfcheck.cu -- exhaustive device checks of the library's own float32
 // math: the fast division inside exp and sigmoid, the double reciprocal
-// behind division by a per-row constant, tanh, and DynamicQuantizeLinear's
-// float32 shortcut (bt_selfcheck in bt_ops.h).
+// and the float32 quotients behind division by a per-row constant, tanh,
+// and DynamicQuantizeLinear's float32 shortcut (bt_selfcheck in bt_ops.h).
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "bt_ops.h"
@@ -85,14 +85,52 @@ __global__ void __launch_bounds__(256) selfcheck_kernel(int kind, uint32_t first
   if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
 }
 
+// kind 7: division by a row constant in float32 (div_row_fast) for the
+// divisor significands first .. first + count - 1 in [1, 2), each against
+// all 2^23 dividend significands in [1, 2).  q is RN(a / b) iff the residual
+// a - b q lies strictly inside half the gap around q (a quotient of floats is
+// never a rounding midpoint, so there are no ties): for the correctly rounded
+// q that residual is a float, which one FMA computes exactly; for any other q
+// the exact residual lies beyond the bound, and so does its rounding.  Below
+// a power of two the gap is half as wide.
+__global__ void __launch_bounds__(256) rowdiv_check_kernel(uint32_t first, uint32_t count,
+                                                           unsigned long long* mismatches) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  unsigned long long bad = 0;
+  if (t < count) {
+    const float b = bits_f(0x3f800000u | (first + t));
+    const float y = __frcp_rn(b);
+#pragma unroll 4
+    for (uint32_t m = 0; m < (1u << 23); ++m) {
+      const float a = bits_f(0x3f800000u | m);
+      const float q = div_row_fast(a, b, y);
+      const uint32_t qb = f_bits(q);
+      const float h = __fmul_rn(b, bits_f((qb & 0x7f800000u) - (24u << 23)));   // b ulp(q) / 2
+      const float r = __fmaf_rn(-b, q, a);
+      const bool ok = r >= 0.0f ? r < h : -r < ((qb & 0x7fffffu) ? h : __fmul_rn(0.5f, h));
+      bad += ok ? 0 : 1;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) bad += __shfl_xor_sync(0xffffffffu, bad, o);
+  if ((threadIdx.x & 31) == 0 && bad) atomicAdd(mismatches, bad);
+}
+
 }  // namespace
 }  // namespace bt
 
 using namespace bt;
 
 extern "C" int bt_selfcheck(int kind, uint32_t first, uint64_t count, unsigned long long* mismatches) {
-  if (kind < 0 || kind > 6) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
+  if (kind < 0 || kind > 7) return set_error(BT_EINVAL, "bt_selfcheck: kind %d", kind);
   if (!mismatches) return set_error(BT_EINVAL, "bt_selfcheck: null counter");
+  if (kind == 7) {
+    if (count > (1ull << 23) || (uint64_t)first + count > (1ull << 23))
+      return set_error(BT_EINVAL, "bt_selfcheck: divisor significands past 2^23");
+    if (count == 0) return BT_OK;
+    const uint32_t n = (uint32_t)count;
+    rowdiv_check_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(first, n, mismatches);
+    return check_launch("bt_selfcheck");
+  }
   if (count > (1ull << 32) || (uint64_t)first + count > (1ull << 32))
     return set_error(BT_EINVAL, "bt_selfcheck: range past 2^32 bit patterns");
   if (count == 0) return BT_OK;

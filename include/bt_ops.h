@@ -351,7 +351,12 @@ int bt_host_math(int kind, const float* in, float* out, int64_t n);
  * only when it is more than one float ulp from the correctly rounded tanh,
  * 6 DynamicQuantizeLinear's float32 shortcut against its exact double path
  * at eight built-in (scale, zero point) pairs (a mismatch per differing
- * pair).  Asynchronous on the set stream.
+ * pair), 7 division by a per-row constant in float32 arithmetic (the
+ * reciprocal's product corrected by one FMA residual step) against the
+ * correctly rounded quotient: for kind 7 first .. first + count - 1 (up to
+ * 2^23) are divisor significands, each checked against all 2^23 dividend
+ * significands (all 2^46 pairs take about half a minute).  Asynchronous on
+ * the set stream.
  * No counterpart in the reference: over all 2^32 inputs it shows that the
  * library's fast division gives the IEEE quotient, hence numpy's result,
  * in every use. */

@@ -62,7 +62,8 @@ def test_errors_set_message(lib):
     assert b"16-byte" in lib.bt_last_error()
     y = _lib.make_tensor(0, np.uint8, (4,))
     assert lib.bt_dynamic_quantize_ranged(ctypes.byref(x), ctypes.byref(y), None, None, None) == -1
-    assert lib.bt_selfcheck(7, 0, 16, None) == -1 and b"kind" in lib.bt_last_error()
+    assert lib.bt_selfcheck(8, 0, 16, None) == -1 and b"kind" in lib.bt_last_error()
+    assert lib.bt_selfcheck(7, 1, 1 << 23, ctypes.c_void_p(16)) == -1 and b"2^23" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 0, 16, None) == -1 and b"null" in lib.bt_last_error()
     assert lib.bt_selfcheck(0, 1, 1 << 32, ctypes.c_void_p(16)) == -1
 

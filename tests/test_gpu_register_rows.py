@@ -63,6 +63,24 @@ def test_register_softmax_rows(gpu_runtime, n, mask_kind):
     assert_same(got.cpu().numpy(), want, f"softmax n={n} mask={mask_kind}")
 
 
+@pytest.mark.parametrize("n", [510, 512])
+def test_register_softmax_quotients_across_the_float_range(gpu_runtime, n):
+    """Rows whose exponentials span every regime of the float32 quotient:
+    values near the row maximum, tiny ones below 2^-60 (which the kernel
+    divides in double), subnormal ones, exact zeros, and rows of equal
+    values (a denominator of n)."""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal((6, 40, n)) * 2).astype(np.float32)
+    x[0] = rng.uniform(-110.0, 0.0, (40, n)).astype(np.float32)      # exps from 1 down to subnormal and 0
+    x[1] = rng.uniform(-45.0, 0.0, (40, n)).astype(np.float32)       # around 2^-60
+    x[2, :, :] = 3.0                                                  # denominator n, every quotient 1 / n
+    x[3, ::2, ::7] = -95.0                                            # a few subnormal exps per row
+    x[4] = (rng.standard_normal((40, n)) * 20).astype(np.float32)    # wide logits
+    x[5, :, n // 2:] = -1e30                                          # half the row exactly zero
+    got = gpu_runtime.softmax(torch.from_numpy(x).cuda(), None, -1)
+    assert_same(got.cpu().numpy(), _oracle(x, None), f"softmax n={n} across the float range")
+
+
 def test_misaligned_rows_take_the_staged_kernel(gpu_runtime):
     rng = np.random.default_rng(9)
     n = 510
@@ -93,7 +111,7 @@ def _oracle_ln(x, skip, bias, gamma, beta, eps):
     return env["y"]
 
 
-@pytest.mark.parametrize("variant", ["plain", "beta", "skip_bias", "skip_nobias", "f16_params", "specials"])
+@pytest.mark.parametrize("variant", ["plain", "beta", "skip_bias", "skip_nobias", "f16_params", "specials", "scales"])
 def test_register_layernorm_768(gpu_runtime, variant):
     """Rows of 768 values, enough of them (2400) for the warp-per-row path,
     which holds them in registers."""
@@ -113,6 +131,15 @@ def test_register_layernorm_768(gpu_runtime, variant):
         x[0, 1, :] = 7.0                 # zero variance: (x - mu) / sqrt(eps)
         x[1, 2, 5] = np.inf
         x[2, 3, 100] = 1e30
+    if variant == "scales":
+        # deviations and deviations over sd outside the float32 quotient's
+        # window [2^-60, 2^60) (divided in double), inside it, and exactly zero
+        x[0, :50] *= np.float32(1e-25)
+        x[0, 50:100] *= np.float32(1e25)
+        x[0, 100:150] *= np.float32(1e-12)
+        x[1, :50, ::3] = 0.5
+        x[1, 50:100] = np.float32(2.0) ** rng.integers(-70, 70, (50, 768)).astype(np.float32)
+        x[2, :20] = np.float32(3.0)
     want = _oracle_ln(x, skip, bias, gamma, beta, eps)
     d = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()   # noqa: E731
     got = gpu_runtime.layernorm(d(x), d(skip), d(bias), d(gamma), d(beta), -1, eps)

@@ -17,7 +17,11 @@ float ulp of the correctly rounded tanh on every input (numpy's float32 tanh
 is within one ulp of that too, so the two stay within the 2-ulp bound of the
 op tests).  DynamicQuantizeLinear's float32 shortcut (a reciprocal product,
 with the exact double quotient near half-integers) must equal the exact path
-on every input at each of eight scales."""
+on every input at each of eight scales.  Division by a per-row constant in
+float32 alone (the correctly rounded reciprocal's product, corrected by one
+FMA residual step) must give the correctly rounded quotient on all 2^46
+pairs of significands, which covers every dividend and divisor inside the
+window where the kernels use it."""
 import ctypes
 
 import pytest
@@ -37,3 +41,12 @@ def test_fast_division_equals_ieee_on_every_input(lib, kind, name):
     _lib.check(lib.bt_selfcheck(kind, 0, 1 << 32, ctypes.c_void_p(count.data_ptr())), "bt_selfcheck")
     torch.cuda.synchronize()
     assert int(count.item()) == 0, f"{name}: {int(count.item())} inputs differ from IEEE division"
+
+
+def test_row_division_in_float32_is_correctly_rounded_on_every_significand_pair(lib):
+    count = torch.zeros(1, dtype=torch.int64, device="cuda")
+    chunk = 1 << 20
+    for first in range(0, 1 << 23, chunk):
+        _lib.check(lib.bt_selfcheck(7, first, chunk, ctypes.c_void_p(count.data_ptr())), "bt_selfcheck")
+    torch.cuda.synchronize()
+    assert int(count.item()) == 0, f"{int(count.item())} (dividend, divisor) pairs differ from RN(a / b)"
