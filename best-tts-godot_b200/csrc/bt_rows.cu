@@ -329,6 +329,24 @@ __global__ void reduce_cols_kernel(ReduceColsArgs a) {
   }
 }
 
+// floor(n / d) for a fixed d and every n < 2^32 by a multiply and a shift
+// (the round-up method of Granlund and Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (below 2^32), floor(n / d) =
+// (umulhi(m, n) + n) >> l, the sum formed in 64 bits.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv fast_div_for(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{d, (uint32_t)m, l};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return (uint32_t)(((uint64_t)__umulhi(f.m, n) + n) >> f.l);
+}
+
 struct SoftmaxArgs {
   const float* x;
   const float* mask;                 // may be null
@@ -339,8 +357,26 @@ struct SoftmaxArgs {
   int64_t mask_lead_st[BT_MAX_RANK]; // mask stride per leading axis (0 = broadcast)
   int64_t mask_col_st;               // mask stride along the softmax axis (0 or 1)
   int32_t mask_row_const;            // 1: every leading stride is 0 (one mask row for all rows)
+  // the leading axes collapsed for the mask row's offset (innermost first;
+  // axes of extent 1 dropped, neighbours merged where the mask's strides
+  // allow): set for fewer than 2^32 rows, read by the warp-row kernels
+  int32_t mnd;
+  FastDiv mdiv[BT_MAX_RANK];
+  int64_t mst[BT_MAX_RANK];
   float* out;
 };
+
+// Offset of row `row`'s mask row (row < 2^32; the collapsed axes above).
+__device__ __forceinline__ long long mask_row_offset(const SoftmaxArgs& a, uint32_t row) {
+  long long moff = 0;
+  uint32_t rem = row;
+  for (int d = 0; d < a.mnd; ++d) {
+    const uint32_t q = fast_div(rem, a.mdiv[d]);
+    moff += (long long)(rem - q * a.mdiv[d].d) * a.mst[d];
+    rem = q;
+  }
+  return moff;
+}
 
 __global__ void softmax_rows_kernel(SoftmaxArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -875,23 +911,9 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
   warp_rows(W, n, a.rows, [&](int64_t row) { return x + row * (int64_t)n; }, [&](int64_t row, float* b) {
     const float* mr = nullptr;
     if (a.mask) {
-      // the mask row of this row: lane 0 unravels the row index (64-bit
-      // division) only when the mask varies along the leading axes
-      long long moff = 0;
-      if (!a.mask_row_const) {
-        if (lane == 0) {
-          // 32-bit division: the host sends this kernel fewer than 2^32 rows
-          uint32_t rem = (uint32_t)row;
-          for (int d = a.lead_rank - 1; d >= 0; --d) {
-            const uint32_t ext = (uint32_t)a.lead_shape[d];
-            const uint32_t c = rem % ext;
-            rem /= ext;
-            moff += (long long)c * a.mask_lead_st[d];
-          }
-        }
-        moff = __shfl_sync(0xffffffffu, moff, 0);
-      }
-      mr = a.mask + moff;
+      // the mask row of this row (the host sends this kernel fewer than
+      // 2^32 rows)
+      mr = a.mask + (a.mask_row_const ? 0ll : mask_row_offset(a, (uint32_t)row));
     }
     // the mask Add (when fused) and the row maximum in one pass.  fmaxf
     // skips NaN where np.max returns it, but the row's result is all NaN
@@ -1117,23 +1139,21 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
         for (int k = 0; k < 8; ++k)
           if (e0 + 8 * k < N) v[k] = pk_add(v[k], mk[k][lane]);
       } else {
-        // this row's mask row (32-bit unravel: the host sends fewer than 2^32 rows)
-        long long moff = 0;
-        if (lane == 0) {
-          uint32_t rem = (uint32_t)row;
-          for (int d = a.lead_rank - 1; d >= 0; --d) {
-            const uint32_t ext = (uint32_t)a.lead_shape[d];
-            const uint32_t c = rem % ext;
-            rem /= ext;
-            moff += (long long)c * a.mask_lead_st[d];
-          }
-        }
-        moff = __shfl_sync(0xffffffffu, moff, 0);
-        const float* mr = a.mask + moff;
+        // this row's mask row (the host sends fewer than 2^32 rows), pairs
+        // loaded as one 8-byte vector where the row is contiguous and aligned
+        const float* mr = a.mask + mask_row_offset(a, (uint32_t)row);
+        if (a.mask_col_st == 1 && ((uintptr_t)mr & 7) == 0) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int e = e0 + 8 * k;
-          if (e < N) v[k] = pk_add(v[k], make_float2(mr[e * a.mask_col_st], mr[(e + 1) * a.mask_col_st]));
+          for (int k = 0; k < 8; ++k) {
+            const int e = e0 + 8 * k;
+            if (e < N) v[k] = pk_add(v[k], __ldg(reinterpret_cast<const float2*>(mr + e)));
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int e = e0 + 8 * k;
+            if (e < N) v[k] = pk_add(v[k], make_float2(mr[e * a.mask_col_st], mr[(e + 1) * a.mask_col_st]));
+          }
         }
       }
     }
@@ -1816,6 +1836,23 @@ extern "C" int bt_softmax(const bt_tensor* x, const bt_tensor* mask, int axis, c
     a.mask_row_const = 1;
     for (int d = 0; d < a.lead_rank; ++d)
       if (a.mask_lead_st[d] != 0) a.mask_row_const = 0;
+    if (rows < (1ll << 32)) {
+      // collapse the leading axes for mask_row_offset: an outer axis whose
+      // mask stride is the inner one's stride times its extent merges into it
+      int64_t ext[BT_MAX_RANK];
+      for (int d = a.lead_rank - 1; d >= 0; --d) {
+        const int64_t e = a.lead_shape[d], st = a.mask_lead_st[d];
+        if (e == 1) continue;
+        if (a.mnd > 0 && st == a.mst[a.mnd - 1] * ext[a.mnd - 1]) {
+          ext[a.mnd - 1] *= e;
+          continue;
+        }
+        ext[a.mnd] = e;
+        a.mst[a.mnd] = st;
+        ++a.mnd;
+      }
+      for (int d = 0; d < a.mnd; ++d) a.mdiv[d] = fast_div_for((uint32_t)ext[d]);
+    }
   }
   // rows of 510 / 512 values, 8-byte aligned: held in registers
   if ((n == 510 || n == 512) && rows < (1ll << 32) && ((uintptr_t)x->data & 7) == 0 &&

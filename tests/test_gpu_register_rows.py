@@ -31,7 +31,8 @@ def _oracle(x, mask):
 
 
 @pytest.mark.parametrize("n", [300, 510, 512])
-@pytest.mark.parametrize("mask_kind", ["row_const", "per_batch", "scalar", "strided", "none"])
+@pytest.mark.parametrize("mask_kind", ["row_const", "per_batch", "per_query", "per_head_query", "offset_view",
+                                       "scalar", "strided", "none"])
 def test_register_softmax_rows(gpu_runtime, n, mask_kind):
     rng = np.random.default_rng(n + len(mask_kind))
     B, H, Q = 3, 4, 37
@@ -48,6 +49,14 @@ def test_register_softmax_rows(gpu_runtime, n, mask_kind):
         mask = np.zeros((B, 1, 1, n), np.float32)
         for b in range(B):
             mask[b, ..., n - 10 * (b + 1):] = -1e4
+    elif mask_kind == "per_query":          # [B, 1, Q, n]: three collapsed axes
+        mask = (rng.standard_normal((B, 1, Q, n)) * 3).astype(np.float32)
+    elif mask_kind == "per_head_query":     # [1, H, Q, n]: H and Q merge into one axis
+        mask = (rng.standard_normal((1, H, Q, n)) * 3).astype(np.float32)
+    elif mask_kind == "offset_view":        # per batch, rows 4 bytes off an 8-byte boundary
+        wide = (rng.standard_normal(B * n + 1) * 3).astype(np.float32)
+        mask = wide[1:].reshape(B, 1, 1, n)
+        mask_dev = torch.from_numpy(wide).cuda()[1:].view(B, 1, 1, n)
     elif mask_kind == "scalar":
         mask = np.array([-3.0], np.float32)
     elif mask_kind == "strided":
