@@ -120,6 +120,19 @@ __device__ __forceinline__ float2 pk_div_nr(float2 a, float2 b) {
   return pk_fma(r, y, q);
 }
 
+// The quotient of numpy's exp, P5(r) / Q2(r), two lanes at a time: the
+// hardware reciprocal approximation of Q2 and one FMA residual correction
+// of the quotient, with no Newton-Raphson step on the reciprocal.  Not a
+// correctly rounded division in general; for exp's own operands (Q2 in
+// [0.9, 1.1], P5 in [0.7, 1.5]) it gives the IEEE quotient on every float32
+// input, which bt_selfcheck (kind 1) checks over all 2^32 of them.
+__device__ __forceinline__ float2 pk_exp_quotient(float2 num, float2 den) {
+  const float2 y = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  const float2 q = pk_mul(num, y);
+  const float2 r = pk_fma(pk_mul(den, pk(-1.0f)), q, num);
+  return pk_fma(r, y, q);
+}
+
 // Both lanes through the scalar np_expf (NaN and the saturated ranges; the
 // scalar function is short, so it stays inline -- no call, no stack frame).
 __device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_expf(x.x), np_expf(x.y)); }
@@ -136,10 +149,10 @@ __device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_
 // returns +0: masked softmax keys, large sigmoid arguments) stays on this
 // path too, computing on 0 and selecting +0 at the end, so a warp whose rows
 // hold such values does not split between the two paths.
-__device__ __forceinline__ float2 pk_np_exp(float2 x) {
-  const float kXmin = -103.97208404541015625f;
-  const bool ux = x.x <= kXmin, uy = x.y <= kXmin;
-  if (!((fabsf(x.x) < 86.0f || ux) && (fabsf(x.y) < 86.0f || uy))) return pk_exp_edge(x);
+constexpr float kExpXmin = -103.97208404541015625f;
+// the fast path proper: ux / uy mark lanes at or below kExpXmin, every other
+// lane lies in (-86, 86)
+__device__ __forceinline__ float2 pk_np_exp_core(float2 x, bool ux, bool uy) {
   x = make_float2(ux ? 0.0f : x.x, uy ? 0.0f : x.y);
   const float kMagic = 12582912.0f;   // 1.5 * 2^23
   // product then sum: lane by lane (two roundings, see pk_add_lanes)
@@ -154,9 +167,28 @@ __device__ __forceinline__ float2 pk_np_exp(float2 x) {
   num = pk_fma(num, r, pk(9.999999999980870924916e-01f));
   float2 den = pk_fma(pk(2.159509375685829852307e-02f), r, pk(-2.742335390411667452936e-01f));
   den = pk_fma(den, r, pk(1.0f));
-  const float2 pq = pk_div_nr(num, den);
+  const float2 pq = pk_exp_quotient(num, den);
   return make_float2(ux ? 0.0f : __uint_as_float(__float_as_uint(pq.x) + (__float_as_uint(t.x) << 23)),
                      uy ? 0.0f : __uint_as_float(__float_as_uint(pq.y) + (__float_as_uint(t.y) << 23)));
+}
+__device__ __forceinline__ float2 pk_np_exp(float2 x) {
+  const bool ux = x.x <= kExpXmin, uy = x.y <= kExpXmin;
+  if (!((fabsf(x.x) < 86.0f || ux) && (fabsf(x.y) < 86.0f || uy))) return pk_exp_edge(x);
+  return pk_np_exp_core(x, ux, uy);
+}
+// pk_np_exp for arguments at most 0 or NaN (softmax's x - max).  The fast
+// path takes [-41, 0] and the underflow range; a lane in between (exp from
+// about 1.6e-18 down to subnormal) or NaN sends both lanes through the
+// scalar function and sets `tiny`: of these exponentials only values of at
+// least 2^-60 (or exact zeros) stay inside the window of the float32 row
+// division (div_row_fast in bt_core.h).
+__device__ __forceinline__ float2 pk_np_exp_nonpos(float2 x, bool& tiny) {
+  const bool ux = x.x <= kExpXmin, uy = x.y <= kExpXmin;
+  if (!((x.x >= -41.0f || ux) && (x.y >= -41.0f || uy))) {
+    tiny = true;
+    return pk_exp_edge(x);
+  }
+  return pk_np_exp_core(x, ux, uy);
 }
 
 // 1 / (1 + exp(-x)) of both lanes, np_sigmoidf step for step: the quotient

@@ -1164,25 +1164,21 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
     for (int k = 0; k < 8; ++k) m = fmaxf(m, fmaxf(v[k].x, v[k].y));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    // exp(x - max), two lanes per instruction (x - m == x + (-m))
+    // exp(x - max), two lanes per instruction (x - m == x + (-m), at most 0
+    // or NaN)
     const float2 nm = pk(-m);
+    bool tiny = false;
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      if (e0 + 8 * k < N) v[k] = pk_np_exp(pk_add(v[k], nm));
+      if (e0 + 8 * k < N) v[k] = pk_np_exp_nonpos(pk_add(v[k], nm), tiny);
     const float total = reg_pw_sum<8, N, 0>(v, RegIdentity());
     const float denom = BT_ADD(0.0f, total);
     // The quotients in float32 (div_row_fast, two lanes at a time).  The
     // denominator lies in [1, 512] (the row's maximum contributes exp(0) = 1)
-    // or is NaN, and every value in [0, 1] or NaN, so only values in
-    // (0, 2^-60) leave the window; +0 gives +0 exactly (0 y = 0, residual
-    // +0) and NaN stays NaN.  A lane holding such a value divides in double.
+    // or is NaN, and each value in [2^-60, 1], +0 (0 y = 0, residual +0:
+    // exactly +0) or NaN (NaN either way) -- unless the exponential set
+    // `tiny`, and then this lane divides in double.
     const float2 nb = pk(-denom), y2 = pk(__frcp_rn(denom));
-    bool tiny = false;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      tiny |= f_bits(v[k].x) - 1u < kRowDivLo - 1u;
-      tiny |= f_bits(v[k].y) - 1u < kRowDivLo - 1u;
-    }
     float* orow = a.out + row * N;
     if (!tiny) {
 #pragma unroll
