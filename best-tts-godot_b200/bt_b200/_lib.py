@@ -97,6 +97,7 @@ SIGNATURES = {
                                          _P(ctypes.c_int), _P(ctypes.c_int64), _P(ctypes.c_int64)]),
     "bt_host_math": (ctypes.c_int, [ctypes.c_int, _P(ctypes.c_float), _P(ctypes.c_float), ctypes.c_int64]),
     "bt_selfcheck": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]),
+    "bt_wait_timeouts": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "bt_dynamic_quantize": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
     "bt_dynamic_quantize_noalloc": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p]),
     "bt_dynamic_quantize_ranged": (ctypes.c_int, [_P(BtTensor), _P(BtTensor), ctypes.c_void_p, ctypes.c_void_p,

@@ -30,6 +30,7 @@
 #include "bt_core.h"
 #include "bt_dq.h"
 #include "bt_pk.h"
+#include "bt_bulk.h"
 
 namespace bt {
 namespace cg = cooperative_groups;
@@ -83,26 +84,26 @@ struct AdainArgs {
 
 __device__ __forceinline__ int phase4(const void* p) { return (int)(((uintptr_t)p >> 2) & 3); }
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
-}
 
 __device__ __forceinline__ float ldf(const void* p, int dt, int64_t i) {
   return dt == BT_F16 ? __half2float(((const __half*)p)[i]) : ((const float*)p)[i];
 }
 
-// Copies n floats g[0..n) into b[0..n) (b shares g's 16-byte phase).
-__device__ __forceinline__ void stage_async(float* b, const float* g, int n) {
+// Copies n floats g[0..n) into b[0..n) (b shares g's 16-byte phase): the
+// aligned interior as one bulk copy completing on `bar` (issued by thread
+// 0), the at most six edge elements by plain loads of threads 32-37.
+__device__ __forceinline__ void stage_bulk(float* b, const float* g, int n, uint64_t* bar) {
   int head = (4 - phase4(g)) & 3;
   if (head > n) head = n;
   const int nvec = (n - head) >> 2;
-  for (int q = threadIdx.x; q < nvec; q += kThreads) cp_async16(b + head + 4 * q, g + head + 4 * q);
-  for (int i = threadIdx.x; i < head; i += kThreads) b[i] = g[i];
-  for (int i = head + 4 * nvec + threadIdx.x; i < n; i += kThreads) b[i] = g[i];
+  const int tail0 = head + 4 * nvec;
+  const int nedge = head + (n - tail0);
+  const int t = (int)threadIdx.x - 32;
+  if (t >= 0 && t < nedge) {
+    const int i = t < head ? t : tail0 + (t - head);
+    b[i] = g[i];
+  }
+  if (threadIdx.x == 0 && nvec > 0) bulk_load(b + head, g + head, 16u * (unsigned)nvec, bar);
 }
 
 // Combines the inner nodes of the tree in hs (warp 0, level by level); the
@@ -307,9 +308,27 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   float* b1 = NSRC > 1 ? sb + A.seg_cap + phase4(g1) : nullptr;
   float* b2 = NSRC > 2 ? sb + 2 * A.seg_cap + phase4(g2) : nullptr;
 
-  stage_async(b0, g0, seg);
-  if (NSRC > 1) stage_async(b1, g1, seg);
-  if (NSRC > 2) stage_async(b2, g2, seg);
+  // the segment of every source by bulk copies completing on one mbarrier
+  __shared__ __align__(8) uint64_t s_bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&s_bar, 1);
+    unsigned bytes = 0;
+    // announce the bytes before the copies: a copy may complete first
+    {
+      auto interior = [&](const float* g) {
+        int h = (4 - phase4(g)) & 3;
+        if (h > seg) h = seg;
+        return 16u * (unsigned)((seg - h) >> 2);
+      };
+      bytes = interior(g0);
+      if (NSRC > 1) bytes += interior(g1);
+      if (NSRC > 2) bytes += interior(g2);
+    }
+    mbar_arrive_expect_tx(&s_bar, bytes);
+  }
+  stage_bulk(b0, g0, seg, &s_bar);
+  if (NSRC > 1) stage_bulk(b1, g1, seg, &s_bar);
+  if (NSRC > 2) stage_bulk(b2, g2, seg, &s_bar);
   // the row constants after the copies are issued: their loads overlap the
   // copies instead of delaying them
 #pragma unroll
@@ -323,12 +342,14 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
       }
     }
   }
-  cp_async_wait_all();
-  // A CTA barrier for the staged rows, the plan and the row constants; with
-  // cs > 1 also the guarantee that every CTA of the cluster runs before any
+  // A CTA barrier for the edge elements, the plan, the row constants and
+  // the mbarrier's initialisation; then every thread waits for the bulk
+  // copies (a wait that gives up is counted, see bt_bulk.h).  With cs > 1
+  // also the guarantee that every CTA of the cluster runs before any
   // distributed shared-memory write below (an arrival without release
   // semantics suffices for that).
   __syncthreads();
+  mbar_wait(&s_bar, 0);
   if (cs > 1) {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
     asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
@@ -346,25 +367,33 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   // constant, see div_by).  Warp 0 sums the tree and derives the row
   // scalars; every other warp waits at the CTA barrier.
   slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
+  // pass 1 stored h into b0; the residual's bulk store below reads it
+  fence_async_shared();
   sync_sums();
   int head = (4 - phase4(g0)) & 3;
   if (head > seg) head = seg;
   const int nvec = (seg - head) >> 2;
+  float* const rs = A.res ? A.res + gofs : nullptr;
+  const bool res_bulk = rs && phase4(rs) == phase4(g0) && nvec > 0;
   if (threadIdx.x < 32) {
     const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
-  } else if (A.res) {
-    // the residual h is complete after the first pass: warps 1.. write it
-    // while warp 0 sums the tree (128-bit where the phases agree)
+  } else if (rs) {
+    // the residual h is complete after the first pass: while warp 0 sums
+    // the tree, thread 32 stores its aligned interior from shared memory in
+    // one bulk copy (b0 is only read from here on; thread 32 waits for the
+    // copy before the CTA exits) and the other threads write the edges
     const int t = (int)threadIdx.x - 32;
     constexpr int kW = kThreads - 32;
-    float* r = A.res + gofs;
-    if (phase4(r) == phase4(g0)) {
-      for (int q = t; q < nvec; q += kW) __stcs((float4*)(r + head + 4 * q), *(const float4*)(b0 + head + 4 * q));
-      for (int i = t; i < head; i += kW) r[i] = b0[i];
-      for (int i = head + 4 * nvec + t; i < seg; i += kW) r[i] = b0[i];
+    if (res_bulk) {
+      if (t == 0) {
+        bulk_store(rs + head, b0 + head, 16u * (unsigned)nvec);
+        bulk_commit();
+      }
+      for (int i = t; i < head; i += kW) rs[i] = b0[i];
+      for (int i = head + 4 * nvec + t; i < seg; i += kW) rs[i] = b0[i];
     } else {
-      for (int i = t; i < seg; i += kW) r[i] = b0[i];
+      for (int i = t; i < seg; i += kW) rs[i] = b0[i];
     }
   }
   __syncthreads();
@@ -489,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
       __syncthreads();   // the shared words are reused by the next output
     }
   }
+  if (res_bulk && threadIdx.x == 32) bulk_wait_all();
 }
 
 // ---- host side -------------------------------------------------------------
@@ -762,3 +792,13 @@ int adain_v3(const bt_adain_args* p, uint32_t* const* range) {
 }
 
 }  // namespace bt
+
+extern "C" int bt_wait_timeouts(uint32_t* count) {
+  if (!count) return bt::set_error(BT_EINVAL, "bt_wait_timeouts: null count");
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, bt::g_bulk_timeouts, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(bt::g_bulk_timeouts, &zero, sizeof(zero));
+  if (e != cudaSuccess) return bt::set_error(BT_ECUDA, "bt_wait_timeouts: %s", cudaGetErrorString(e));
+  *count = v;
+  return BT_OK;
+}

@@ -254,6 +254,13 @@ int bt_adain_snake(const bt_adain_args* a);
  * replaces: the minmax dispatch of executor.gd:1224-1230 (its pass over the
  *           Snake output) for each quantised conv input. */
 int bt_adain_snake_range(const bt_adain_args* a, uint32_t* range);
+/* The number of bounded waits on bulk (TMA) copies in bt_adain_snake /
+ * bt_adain_snake_range kernels that gave up since the last call (each such
+ * wait records itself and lets its kernel run on with unfinished data, so a
+ * copy that never lands cannot hang the GPU); the count is then reset.
+ * Synchronous (waits for the device).  *count == 0 after a run means every
+ * copy completed.  No counterpart in the reference. */
+int bt_wait_timeouts(uint32_t* count);
 
 /* ---- residual mean + LeakyRelu (end of a generator stage) ---------------
  * out = leaky((((a0 + b0) + (a1 + b1)) + (a2 + b2)) / 3, slope) elementwise

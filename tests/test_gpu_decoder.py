@@ -295,3 +295,14 @@ def test_host_pipeline_matches_run_host(lib):
     pipe.finish()
     torch.cuda.synchronize()
     assert torch.equal(hout.view(torch.int32), want.view(torch.int32))
+
+
+def test_zz_every_bulk_copy_completed(lib):
+    """The AdaIN kernels stage rows with bulk copies behind bounded waits; a
+    wait that gave up would have counted itself (none may have, after the
+    fused-stream tests above)."""
+    import ctypes
+    from bt_b200 import _lib
+    n = ctypes.c_uint32(99)
+    _lib.check(lib.bt_wait_timeouts(ctypes.byref(n)), "bt_wait_timeouts")
+    assert n.value == 0
