@@ -4,15 +4,17 @@
 // A row of T values (T up to 49152) is cut at pairwise-tree leaf boundaries
 // into `cs` contiguous segments, one per CTA of a cluster of cs CTAs.  Each
 // CTA
-//   1. stages its segment of every source into shared memory with cp.async
-//      (16-byte global->shared copies, all in flight at once, no registers);
+//   1. stages its segment of every source into shared memory with one bulk
+//      (TMA) copy per source, completing on an mbarrier;
 //   2. sums its leaves of h = src0 + src1 + src2 (numpy's eight-accumulator
-//      leaf sum, two lanes per leaf) and writes each leaf sum into the tree
-//      array of every CTA of the cluster (distributed shared memory);
-//   3. after a cluster barrier, combines the tree (one warp, level by level)
-//      -> the exact numpy mean; the same for the squared deviations -> the
-//      variance;
-//   4. writes its segment of the residual and of every output.
+//      leaf sum, two lanes per leaf) and stores each leaf sum into the tree
+//      array of every CTA of the cluster with st.async, which completes
+//      four bytes on the receiving CTA's mbarrier;
+//   3. waits on its own mbarrier for all leaf sums of the row (no cluster
+//      barrier), combines the tree (one warp) -> the exact numpy mean; the
+//      same for the squared deviations -> the variance;
+//   4. writes its segment of the residual (a bulk copy out of shared memory)
+//      and of every output.
 // HBM sees each input once and each output once.  The pairwise plan (sorted
 // leaves, heap ids, inner-node bitmask) depends on T only; the host computes
 // it once per T and passes it in the kernel's parameter block, so no CTA
@@ -56,6 +58,7 @@ constexpr int kMaxT = 49152;
 struct SlotPlan {
   int32_t T, D, cs;
   int32_t perfect;                     // 1: every leaf at depth D (leaf i = heap id 2^D + i)
+  int32_t nleaves;                     // leaves of the whole row (every rank's)
   int32_t rank_e[kMaxCluster + 1];
   int32_t rank_slot[kMaxCluster + 1];
   uint32_t inner[kMaxIds / 32];        // bit h: heap node h is an inner node
@@ -186,14 +189,16 @@ __device__ __forceinline__ float2 shfl_xor2(unsigned mask, float2 v, int m) {
 // a[j]); lanes then combine them with xor shuffles over lane bits 0, 1, 2 --
 // numpy's bracket ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), float addition being
 // commutative -- and add the len % 8 remainder left to right (a leaf shorter
-// than 8 is the remainder alone, summed from +0.0).  Lanes j < cs write the
-// leaf sums into hs[id] of cluster rank j.
+// than 8 is the remainder alone, summed from +0.0).  Lanes j < cs store the
+// leaf sums into hs[id] of cluster rank j with st.async, each store
+// completing 4 bytes on that rank's mbarrier `bar` (hs and bar are this
+// CTA's shared addresses; every rank uses the same layout).
 //   pass 1 (SQ false): leaf value h = src0 (+ src1 (+ src2)); with NSRC > 1 h
 //     is also stored back into b0 for the later passes;
 //   pass 2 (SQ true, NSRC 1): (h - mu)^2.
 template <int NSRC, bool SQ>
 __device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0, const float* b1, const float* b2,
-                                          float mu, float* hs, cg::cluster_group& cluster, int cs) {
+                                          float mu, unsigned hs, unsigned bar, int cs) {
   const int j = threadIdx.x & 7;
   const unsigned gmask = 0xffu << (threadIdx.x & 24);
   const float2 nmu = pk(-mu);
@@ -255,10 +260,10 @@ __device__ __forceinline__ void slot_pass(const uint32_t* sw, int ns, float* b0,
       acc.y = __shfl_sync(gmask, acc.y, 0, 8);
     }
     if (j < cs) {
-      float* dst = cluster.map_shared_rank(hs, j);
-      dst[w1 & 1023u] = acc.x;
+      const unsigned dst = cluster_addr(hs, (unsigned)j), rbar = cluster_addr(bar, (unsigned)j);
+      st_async_f32(dst + 4u * (w1 & 1023u), acc.x, rbar);
       const unsigned idb = (w1 >> 10) & 1023u;
-      if (idb) dst[idb] = acc.y;
+      if (idb) st_async_f32(dst + 4u * idb, acc.y, rbar);
     }
   }
 }
@@ -308,10 +313,17 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   float* b1 = NSRC > 1 ? sb + A.seg_cap + phase4(g1) : nullptr;
   float* b2 = NSRC > 2 ? sb + 2 * A.seg_cap + phase4(g2) : nullptr;
 
-  // the segment of every source by bulk copies completing on one mbarrier
+  // the segment of every source by bulk copies completing on one mbarrier;
+  // the leaf sums of the two tree passes arrive from every rank by st.async
+  // on two more (4 bytes per leaf of the row each, expected from the start)
   __shared__ __align__(8) uint64_t s_bar;
+  __shared__ __align__(8) uint64_t s_sum_bar[2];
   if (threadIdx.x == 0) {
     mbar_init(&s_bar, 1);
+    mbar_init(&s_sum_bar[0], 1);
+    mbar_init(&s_sum_bar[1], 1);
+    mbar_arrive_expect_tx(&s_sum_bar[0], 4u * (unsigned)A.P.nleaves);
+    mbar_arrive_expect_tx(&s_sum_bar[1], 4u * (unsigned)A.P.nleaves);
     unsigned bytes = 0;
     // announce the bytes before the copies: a copy may complete first
     {
@@ -329,6 +341,10 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   stage_bulk(b0, g0, seg, &s_bar);
   if (NSRC > 1) stage_bulk(b1, g1, seg, &s_bar);
   if (NSRC > 2) stage_bulk(b2, g2, seg, &s_bar);
+  // every CTA of the cluster arrives once its mbarriers are initialised (no
+  // release semantics needed beyond the initialisation fence); the wait
+  // comes before the first st.async below
+  if (cs > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
   // the row constants after the copies are issued: their loads overlap the
   // copies instead of delaying them
 #pragma unroll
@@ -343,39 +359,28 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
     }
   }
   // A CTA barrier for the edge elements, the plan, the row constants and
-  // the mbarrier's initialisation; then every thread waits for the bulk
-  // copies (a wait that gives up is counted, see bt_bulk.h).  With cs > 1
-  // also the guarantee that every CTA of the cluster runs before any
-  // distributed shared-memory write below (an arrival without release
-  // semantics suffices for that).
+  // the mbarriers' initialisation; then every thread waits for the bulk
+  // copies (a wait that gives up is counted, see bt_bulk.h), and with
+  // cs > 1 for every CTA of the cluster to have initialised its mbarriers.
   __syncthreads();
   mbar_wait(&s_bar, 0);
-  if (cs > 1) {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
-    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
-  }
-  // Leaf sums written into other CTAs' shared memory become visible to them
-  // at a full cluster barrier (release / acquire); a cluster of one needs
-  // only the CTA barrier.
-  auto sync_sums = [&]() {
-    if (cs > 1) cluster.sync();
-    else __syncthreads();
-  };
+  if (cs > 1) asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 
   // ReduceMean(h).  np.mean: RN32(RN64(sum) / T), computed as
   // RN32(RN64(sum * RN64(1/T))) -- the same float (division by a per-row
   // constant, see div_by).  Warp 0 sums the tree and derives the row
   // scalars; every other warp waits at the CTA barrier.
-  slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, hs1, cluster, cs);
+  slot_pass<NSRC, false>(sw, ns, b0, b1, b2, 0.0f, smem_u32(hs1), smem_u32(&s_sum_bar[0]), cs);
   // pass 1 stored h into b0; the residual's bulk store below reads it
   fence_async_shared();
-  sync_sums();
+  __syncthreads();
   int head = (4 - phase4(g0)) & 3;
   if (head > seg) head = seg;
   const int nvec = (seg - head) >> 2;
   float* const rs = A.res ? A.res + gofs : nullptr;
   const bool res_bulk = rs && phase4(rs) == phase4(g0) && nvec > 0;
   if (threadIdx.x < 32) {
+    mbar_wait(&s_sum_bar[0], 0);   // every rank's leaf sums
     const float sum = tree_total(hs1, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) s_mu = div_by(BT_ADD(0.0f, sum), A.rT);
   } else if (rs) {
@@ -399,9 +404,9 @@ __global__ void __launch_bounds__(kThreads, 4) adain_cluster_kernel(AdainArgs A)
   __syncthreads();
   const float mu = s_mu;
   // Sub, Mul(d, d), ReduceMean, Add eps, Sqrt
-  slot_pass<1, true>(sw, ns, b0, nullptr, nullptr, mu, hs2, cluster, cs);
-  sync_sums();
+  slot_pass<1, true>(sw, ns, b0, nullptr, nullptr, mu, smem_u32(hs2), smem_u32(&s_sum_bar[1]), cs);
   if (threadIdx.x < 32) {
+    mbar_wait(&s_sum_bar[1], 0);
     const float ssq = tree_total(hs2, inner, A.P.D, A.P.perfect != 0);
     if (threadIdx.x == 0) {
       const float var = div_by(BT_ADD(0.0f, ssq), A.rT);
@@ -591,6 +596,7 @@ const ClusterPlan& cluster_plan(int T, int cs) {
   cp.P.D = hp.D;
   cp.P.cs = cs;
   cp.P.perfect = ((int64_t)hp.off.size() == (1ll << hp.D)) ? 1 : 0;
+  cp.P.nleaves = (int32_t)hp.off.size();
   for (int i = 0; i < kMaxIds / 32; ++i) cp.P.inner[i] = hp.inner[i];
   std::vector<int> first;
   bool ok = rank_split(hp, cs, first) && (2 << hp.D) <= kMaxIds;
@@ -651,6 +657,11 @@ const ClusterPlan& cluster_plan(int T, int cs) {
   }
   cp.P.rank_e[cs] = T;
   cp.P.rank_slot[cs] = n_slots;
+  // every leaf in exactly one slot: each rank then receives 4 * nleaves
+  // bytes of leaf sums per pass, the count its mbarriers expect
+  int stored = 0;
+  for (int i = 0; ok && i < n_slots; ++i) stored += ((cp.P.w1[i] >> 10) & 1023u) ? 2 : 1;
+  if (stored != cp.P.nleaves) ok = false;
   cp.ok = ok;
   return cache.emplace(key, cp).first->second;
 }

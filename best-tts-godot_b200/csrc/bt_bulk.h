@@ -62,6 +62,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsign
   return false;
 }
 
+// The address of the same shared-memory location in CTA `rank` of this
+// cluster (a shared::cluster address).
+__device__ __forceinline__ unsigned cluster_addr(unsigned local, unsigned rank) {
+  unsigned r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+// Stores v at the shared::cluster address `addr` (any CTA of the cluster,
+// this one included) and completes 4 bytes of the transaction count of the
+// mbarrier at shared::cluster address `bar` (in that same CTA): a receiver
+// that waits on its own mbarrier for the bytes it expects needs no cluster
+// barrier.
+__device__ __forceinline__ void st_async_f32(unsigned addr, float v, unsigned bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];\n" ::"r"(addr),
+               "r"(__float_as_uint(v)), "r"(bar)
+               : "memory");
+}
+
 // Orders this thread's earlier (generic) shared-memory writes before later
 // reads of the same bytes by bulk copies (the async proxy).
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
