@@ -66,6 +66,8 @@ _UNARY_NP = {"Sqrt": np.sqrt, "Exp": np.exp, "Sin": np.sin, "Cos": np.cos, "Atan
 COMPARE = {"Greater": "GREATER", "Less": "LESS", "GreaterOrEqual": "GEQ"}
 _BINARY = {"Add": "ADD", "Sub": "SUB", "Mul": "MUL", "Div": "DIV", "Pow": "POW"}
 _F16_TWO = np.array(2.0, dtype=np.float16)   # the Snake exponent constant of the graph
+_SAME = object()   # a cached Cast whose result is its input
+OP_NAMES = {v: k for k, v in OP.items()}
 
 
 def as_cuda_device(device):
@@ -159,8 +161,10 @@ class BtRuntime:
         self.lib = load()
         with torch.cuda.device(self.device):
             check(self.lib.bt_init(self.device.index), "bt_init")
+        self._index = self.device.index
         self._consts = {}
         self._ew_plans = {}
+        self._node_plans = {}   # node signature -> launch plan (see dispatch)
         self._scalars = {}
         self.launches = 0
 
@@ -210,6 +214,10 @@ class BtRuntime:
         per such signature (numpy's result layout, the descriptors, the
         attribute block) and reused: a call then allocates the result, writes
         the pointers into the prepared descriptors and launches."""
+        return self._launch_plan(self._ew_plan(opname, inputs, out_shape, out_dt, compute_dt, alpha), inputs)
+
+    def _ew_plan(self, opname, inputs, out_shape, out_dt, compute_dt, alpha=0.0):
+        """The prepared launch of one element-wise signature (cached)."""
         key = (opname, tuple(out_shape), out_dt, compute_dt, alpha,
                tuple((t.dtype, t.shape, t.stride()) for t in inputs))
         plan = self._ew_plans.get(key)
@@ -218,16 +226,30 @@ class BtRuntime:
             if len(self._ew_plans) >= 8192:
                 self._ew_plans.clear()
             self._ew_plans[key] = plan
+        return plan
+
+    def _launch_plan(self, plan, inputs):
+        """Allocates the result of a prepared launch, writes the data
+        pointers into its descriptors and launches it."""
         alloc_shape, tdt, back, code, descs, od, attrs, numel = plan
         out = torch.empty(alloc_shape, dtype=tdt, device=self.device)
         if numel:
             for i, t in enumerate(inputs):
                 descs[i].data = t.data_ptr()
             od.data = out.data_ptr()
-            self._stream()
-            check(self.lib.bt_elementwise(code, len(inputs), descs, od, attrs), f"bt_elementwise({opname})")
+            lib = self.lib
+            lib.bt_set_stream(_raw_stream(self._index))   # always BT_OK
+            rc = lib.bt_elementwise(code, len(inputs), descs, od, attrs)
+            if rc:
+                check(rc, f"bt_elementwise({OP_NAMES.get(code, code)})")
             self.launches += 1
         return out if back is None else out.permute(back)
+
+    def _remember(self, key, plan):
+        """Caches the launch plan of a node signature (dispatch's fast path)."""
+        if len(self._node_plans) >= 8192:
+            self._node_plans.clear()
+        self._node_plans[key] = plan
 
     def _ew_prepare(self, opname, inputs, out_shape, out_dt, compute_dt, alpha):
         out_shape = tuple(int(v) for v in out_shape)
@@ -364,9 +386,20 @@ class BtRuntime:
 
     # ---- the op table -----------------------------------------------------------------
     def dispatch(self, op, node_input, node_output, at, env):
+        # The most frequent nodes (binary and unary element-wise ops, Cast)
+        # first, without the helpers below: once a node signature -- the op
+        # and each device input's dtype, shape and strides -- has run, its
+        # launch plan (numpy's result dtype and layout included) is cached,
+        # and the node costs a lookup, the result's allocation and the launch.
         if op in _BINARY:
-            # the most frequent nodes, without the helpers below
             x, y = env[node_input[0]], env[node_input[1]]
+            cached = type(x) is torch.Tensor and type(y) is torch.Tensor and x.is_cuda and y.is_cuda
+            if cached:
+                key = (op, x.dtype, x.shape, x.stride(), y.dtype, y.shape, y.stride())
+                plan = self._node_plans.get(key)
+                if plan is not None:
+                    env[node_output[0]] = self._launch_plan(plan, (x, y))
+                    return
             if not isinstance(x, torch.Tensor) or not x.is_cuda:
                 x = self.to_device(x)
             if not isinstance(y, torch.Tensor) or not y.is_cuda:
@@ -375,8 +408,60 @@ class BtRuntime:
             dt = _binary_result(op, a, b)
             if op == "Pow" and dt.kind != "f":
                 raise NotImplementedError("integer Pow is not on the GPU path")
-            env[node_output[0]] = self.elementwise(_BINARY[op], [x, y], _bshape(tuple(x.shape), tuple(y.shape)),
-                                                   dt, self._compute(dt))
+            plan = self._ew_plan(_BINARY[op], [x, y], _bshape(tuple(x.shape), tuple(y.shape)), dt, self._compute(dt))
+            if cached:
+                self._remember(key, plan)
+            env[node_output[0]] = self._launch_plan(plan, (x, y))
+            return
+        if op in UNARY:
+            x = env[node_input[0]]
+            cached = type(x) is torch.Tensor and x.is_cuda
+            if cached:
+                key = (op, x.dtype, x.shape, x.stride())
+                plan = self._node_plans.get(key)
+                if plan is not None:
+                    env[node_output[0]] = self._launch_plan(plan, (x,))
+                    return
+            x = self.to_device(x)
+            a = _wide(np_dtype(x))
+            if op == "Erf":
+                dt = np.dtype(np.float32) if a == np.float32 else np.dtype(np.float64)
+                if a.kind not in "fiub":
+                    raise TypeError(f"Erf of {a}")
+            else:
+                dt = _UNARY_NP[op](_probe(a)).dtype
+            plan = self._ew_plan(UNARY[op], [x], x.shape, dt, self._compute(dt))
+            if cached:
+                self._remember(key, plan)
+            env[node_output[0]] = self._launch_plan(plan, (x,))
+            return
+        if op == "Cast":                                        # ref :572-578
+            x = env[node_input[0]]
+            cached = type(x) is torch.Tensor and x.is_cuda
+            if cached:
+                key = (op, at["to"], x.dtype, x.shape, x.stride())
+                plan = self._node_plans.get(key)
+                if plan is not None:
+                    env[node_output[0]] = x if plan is _SAME else self._launch_plan(plan, (x,))
+                    return
+            x = self.to_device(x)
+            target = np.dtype(ONNX_TO_NUMPY[at["to"]])
+            if target == np.float16:
+                target = np.dtype(np.float32)
+            if np_dtype(x) == target and self._physical(x)[0].is_contiguous():
+                # astype to the dtype x already has: numpy copies the same
+                # values in the same axis order, and graph values are never
+                # written after they are made, so x itself serves (half of
+                # the model's Casts are float32 -> float32 once fp16 targets
+                # are elided, one before every DynamicQuantizeLinear)
+                plan, out = _SAME, x
+            else:
+                src = _wide(np_dtype(x))
+                plan = self._ew_plan("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
+                out = self._launch_plan(plan, (x,))
+            if cached:
+                self._remember(key, plan)
+            env[node_output[0]] = out
             return
 
         def arg(i, default=None):
@@ -397,16 +482,6 @@ class BtRuntime:
                 raise NotImplementedError("integer Pow is not on the GPU path")
             name = {"Add": "ADD", "Sub": "SUB", "Mul": "MUL", "Div": "DIV", "Pow": "POW"}[op]
             out = self.elementwise(name, [x, y], shape, dt, self._compute(dt))
-        elif op in UNARY:
-            x = dev(0)
-            a = _wide(np_dtype(x))
-            if op == "Erf":
-                dt = np.dtype(np.float32) if a == np.float32 else np.dtype(np.float64)
-                if a.kind not in "fiub":
-                    raise TypeError(f"Erf of {a}")
-            else:
-                dt = _UNARY_NP[op](_probe(a)).dtype
-            out = self.elementwise(UNARY[op], [x], x.shape, dt, self._compute(dt))
         elif op == "LeakyRelu":
             x = dev(0)
             a = _wide(np_dtype(x))
@@ -448,21 +523,6 @@ class BtRuntime:
             dt = np.where(_probe(np.bool_), _probe(np_dtype(x)), _probe(np_dtype(y))).dtype
             shape = np.broadcast_shapes(tuple(c.shape), tuple(x.shape), tuple(y.shape))
             out = self.elementwise("WHERE", [c, x, y], shape, dt, self._cast_compute_where(dt))
-        elif op == "Cast":                                      # ref :572-578
-            x = dev(0)
-            target = np.dtype(ONNX_TO_NUMPY[at["to"]])
-            if target == np.float16:
-                target = np.dtype(np.float32)
-            if np_dtype(x) == target and self._physical(x)[0].is_contiguous():
-                # astype to the dtype x already has: numpy copies the same
-                # values in the same axis order, and graph values are never
-                # written after they are made, so x itself serves (half of
-                # the model's Casts are float32 -> float32 once fp16 targets
-                # are elided, one before every DynamicQuantizeLinear)
-                out = x
-            else:
-                src = _wide(np_dtype(x))
-                out = self.elementwise("IDENTITY", [x], x.shape, target, self._cast_compute(src, target))
         elif op == "DequantizeLinear":                          # ref :631-636
             q, scale, zp = dev(0), dev(1), dev(2)
             out = self.dequantize(q, scale, zp)
