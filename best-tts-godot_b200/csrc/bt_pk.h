@@ -147,13 +147,14 @@ __device__ __forceinline__ float2 pk_exp_edge(float2 x) { return make_float2(np_
 // by adding k << 23 to the bits of pq.
 // A lane at or below numpy's underflow bound (-103.972..., where np_expf
 // returns +0: masked softmax keys, large sigmoid arguments) stays on this
-// path too, computing on 0 and selecting +0 at the end, so a warp whose rows
-// hold such values does not split between the two paths.
+// path too, selecting +0 at the end, so a warp whose rows hold such values
+// does not split between the two paths.
 constexpr float kExpXmin = -103.97208404541015625f;
 // the fast path proper: ux / uy mark lanes at or below kExpXmin, every other
-// lane lies in (-86, 86)
+// lane lies in (-86, 86).  A marked lane computes on its own argument
+// (infinite or NaN intermediates included: no float operation traps) and
+// its result is replaced by +0 at the end.
 __device__ __forceinline__ float2 pk_np_exp_core(float2 x, bool ux, bool uy) {
-  x = make_float2(ux ? 0.0f : x.x, uy ? 0.0f : x.y);
   const float kMagic = 12582912.0f;   // 1.5 * 2^23
   // product then sum: lane by lane (two roundings, see pk_add_lanes)
   const float2 t = pk_add_lanes(pk_mul(x, pk(1.442695040888963407359924681001892137f)), pk(kMagic));

@@ -995,6 +995,14 @@ __global__ void __launch_bounds__(256) wrow_softmax_kernel(WSoftmaxArgs A) {
 // no plan: every index is a constant.
 __host__ __device__ constexpr int pw_split_c(int n) { return n / 2 - (n / 2) % 8; }
 
+// max of three floats in one instruction (sm_100); NaN operands are skipped
+// as fmaxf skips them
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 struct RegIdentity {
   static constexpr bool kPacked = true;
   __device__ __forceinline__ float2 operator()(float2 v) const { return v; }
@@ -1119,13 +1127,14 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
   const int64_t stride = (int64_t)gridDim.x * kWarpsPerCta;
   int64_t row = (int64_t)blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
   float2 nx[8];
+  // slots 0-6 lie inside every row of 510 or 512 values (e0 + 48 <= 502);
+  // only slot 7 of the last lanes can pass the end
+  static_assert(N >= 503, "slots 0-6 in bounds");
   auto load_row = [&](int64_t r) {
-    const float* xr = a.x + r * N;
+    const float2* xr = reinterpret_cast<const float2*>(a.x + r * N + e0);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int e = e0 + 8 * k;
-      nx[k] = e < N ? __ldcs(reinterpret_cast<const float2*>(xr + e)) : make_float2(-INFINITY, -INFINITY);
-    }
+    for (int k = 0; k < 8; ++k)
+      nx[k] = (k < 7 || e0 + 8 * k < N) ? __ldcs(xr + 4 * k) : make_float2(-INFINITY, -INFINITY);
   };
   if (row < a.rows) load_row(row);
   for (; row < a.rows; row += stride) {
@@ -1137,7 +1146,7 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
       if (mconst) {
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          if (e0 + 8 * k < N) v[k] = pk_add(v[k], mk[k][lane]);
+          v[k] = pk_add(v[k], mk[k][lane]);   // (past the row: -inf + 0)
       } else {
         // this row's mask row (the host sends fewer than 2^32 rows), pairs
         // loaded as one 8-byte vector where the row is contiguous and aligned
@@ -1146,13 +1155,13 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int e = e0 + 8 * k;
-            if (e < N) v[k] = pk_add(v[k], __ldg(reinterpret_cast<const float2*>(mr + e)));
+            if (k < 7 || e < N) v[k] = pk_add(v[k], __ldg(reinterpret_cast<const float2*>(mr + e)));
           }
         } else {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int e = e0 + 8 * k;
-            if (e < N) v[k] = pk_add(v[k], make_float2(mr[e * a.mask_col_st], mr[(e + 1) * a.mask_col_st]));
+            if (k < 7 || e < N) v[k] = pk_add(v[k], make_float2(mr[e * a.mask_col_st], mr[(e + 1) * a.mask_col_st]));
           }
         }
       }
@@ -1161,7 +1170,7 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
     // wrow_softmax_kernel)
     float m = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) m = fmaxf(m, fmaxf(v[k].x, v[k].y));
+    for (int k = 0; k < 8; ++k) m = max3f(m, v[k].x, v[k].y);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     // exp(x - max), two lanes per instruction (x - m == x + (-m), at most 0
@@ -1170,7 +1179,7 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
     bool tiny = false;
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      if (e0 + 8 * k < N) v[k] = pk_np_exp_nonpos(pk_add(v[k], nm), tiny);
+      v[k] = pk_np_exp_nonpos(pk_add(v[k], nm), tiny);   // (past the row: exp(-inf) = +0)
     const float total = reg_pw_sum<8, N, 0>(v, RegIdentity());
     const float denom = BT_ADD(0.0f, total);
     // The quotients in float32 (div_row_fast, two lanes at a time).  The
@@ -1179,20 +1188,16 @@ __global__ void __launch_bounds__(256, 4) wrow_softmax_reg_kernel(SoftmaxArgs a)
     // exactly +0) or NaN (NaN either way) -- unless the exponential set
     // `tiny`, and then this lane divides in double.
     const float2 nb = pk(-denom), y2 = pk(__frcp_rn(denom));
-    float* orow = a.out + row * N;
+    float2* orow = reinterpret_cast<float2*>(a.out + row * N + e0);
     if (!tiny) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int e = e0 + 8 * k;
-        if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), pk_div_row_fast(v[k], nb, y2));
-      }
+      for (int k = 0; k < 8; ++k)
+        if (k < 7 || e0 + 8 * k < N) __stcs(orow + 4 * k, pk_div_row_fast(v[k], nb, y2));
     } else {
       const double rd = recip_d(denom);
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int e = e0 + 8 * k;
-        if (e < N) __stcs(reinterpret_cast<float2*>(orow + e), make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
-      }
+      for (int k = 0; k < 8; ++k)
+        if (k < 7 || e0 + 8 * k < N) __stcs(orow + 4 * k, make_float2(div_by(v[k].x, rd), div_by(v[k].y, rd)));
     }
   }
 }

@@ -121,6 +121,46 @@ def test_adain_snake_large_and_nonfinite_rows(gpu_runtime, monkeypatch, path, n_
         assert_same(res, h_want, "residual")
 
 
+@pytest.mark.parametrize("path", ["cluster", "one_cta"])
+@pytest.mark.parametrize("n_src", [1, 2])
+def test_adain_snake_rows_across_the_division_window(gpu_runtime, monkeypatch, path, n_src):
+    """Rows whose deviations (h - mu) and standard deviations fall inside and
+    outside the float32 division's window [2^-60, 2^60): tiny rows (1e-25,
+    where sd is sqrt(eps)), huge rows (1e25: sd beyond the window), constant
+    rows (every deviation exactly zero), rows with values exactly at the mean
+    and rows spanning many binades."""
+    if path == "one_cta":
+        monkeypatch.setenv("BT_ADAIN_ONE_CTA", "1")
+    rt = gpu_runtime
+    rng = np.random.default_rng(91 + n_src)
+    B, Cc, T = 2, 6, 3001
+    srcs = [(rng.standard_normal((B, Cc, T)) * 2).astype(np.float32) for _ in range(n_src)]
+    srcs[0][0, 0] *= np.float32(1e-25)
+    srcs[0][0, 1] *= np.float32(1e25)
+    srcs[0][0, 2] = np.float32(0.75)
+    srcs[0][1, 0] = np.float32(2.0) ** rng.integers(-70, 70, T).astype(np.float32)
+    srcs[0][1, 1, ::2] = np.float32(1.0)
+    srcs[0][1, 1, 1::2] = np.float32(-1.0)
+    for s_ in srcs[1:]:
+        s_[0, :3] = 0.0                  # keep the planted rows as planted
+        s_[1, :2] = 0.0
+    fc = rng.standard_normal((B, 2 * Cc, 1)).astype(np.float32)
+    alpha = rng.uniform(0.5, 1.5, (1, Cc, 1)).astype(np.float16)
+    inv = (1.0 / alpha.astype(np.float64)).astype(np.float16)
+    eps = np.array(1e-5, np.float16)
+    h_want, z_want = oracle_adain_snake(srcs, fc, alpha, inv, eps, True)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    fcd = d(fc[:, :, 0])
+    gain = rt.elementwise("ADD", [fcd[:, :Cc], d(np.array(1.0, np.float16))], (B, Cc), np.float32, np.float32)
+    res = torch.empty((B, Cc, T), dtype=torch.float32, device="cuda") if n_src > 1 else None
+    out = rt.adain_snake([d(s) for s in srcs], gain, fcd[:, Cc:], np.float32(eps), d(alpha.reshape(-1)),
+                         d(inv.reshape(-1)), res=res)
+    torch.cuda.synchronize()
+    assert_same(out[0], z_want, "adain/snake output")
+    if res is not None:
+        assert_same(res, h_want, "residual")
+
+
 def test_adain_three_outputs_share_norm(gpu_runtime):
     rt = gpu_runtime
     rng = np.random.default_rng(5)
