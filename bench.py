@@ -6,19 +6,22 @@ Headline workload: the ISTFTNet generator's elementwise /
 broadcast / reduction op stream for ONE fixed batch of 64 utterances,
 features [512, 400] -> stages [256, 4000] and [128, 24001], conv and fc
 outputs as seeded stand-ins resident in HBM.  One step = the whole stream for
-the batch (49 kernel launches per GPU).  With torchrun (N > 1) the batch is
-split by utterance (64 / N per rank, shard.split_utterances; "scaling":
-"strong"), every rank runs its share through its own FusedDecoder with no
-collective on the data path, and the job's time is the max over ranks.  At
-N > 1 the weak-scaling figure (64 utterances on every rank) is reported
-beside it under "weak".
+the batch (49 kernel launches per decoder).  With torchrun (N > 1) the batch
+is split by utterance (64 / N per rank, shard.split_utterances; "scaling":
+"strong"), every rank runs its share with no collective on the data path,
+and the job's time is the max over ranks.  A rank with 2-32 utterances
+splits them again over two FusedDecoders on two concurrent CUDA streams
+(--streams), which keeps the GPU busy where one decoder's launches are too
+small to.  At N > 1 the weak-scaling figure (64 utterances on every rank)
+is reported beside it under "weak".
 
 Printed (rank 0, one JSON line): utt/s of the whole batch from CUDA events
 with inputs resident; ``e2e`` through FusedDecoder.host_pipeline with pinned
 host buffers (features + fc outputs in, final stage output out, every step)
 and ``e2e_limit``, which names what bounds it (the device step or the
 device-to-host copy of the result); ``roofline`` for the dominant kernel
-(bt_adain_snake) from per-launch CUDA events; ``cpu_baseline`` = the numpy
+(bt_adain_snake) from per-launch CUDA events, taken in a second pass of the
+same steps (events between launches would slow the timed one); ``cpu_baseline`` = the numpy
 oracle on the host cores; ``per_op`` = each BASELINE op config c1-c4 (GB/s,
 fraction of the measured HBM peak and of the nominal 8 TB/s) plus a >= 256 MB
 sweep, each next to the oracle's single-core numpy time; ``clocks`` sampled
@@ -61,19 +64,23 @@ def rank_batches(total, n):
     return [shard.split_utterances(total, n, r)[1] for r in range(n)]
 
 
-def config(args, n):
+def config(args, n, groups=None):
     from bt_b200.decoder import stage_shapes
     per = rank_batches(args.batch, n)
+    if groups is None:
+        groups = stream_groups(max(per), getattr(args, "streams", 0))
     gpu_bytes = max(per) * 128 * (args.t0 * 60 + 1) * 4
     return {"workload": "c5: batched Kokoro-82M ISTFTNet decoder-stage op stream (BASELINE configs[4])",
             "global_batch": args.batch, "batch_per_gpu": max(per), "batch_split": per, "t0": args.t0,
             "stage_shapes": [[c, t] for (_, _, c, t) in stage_shapes(args.t0)],
             "parallelism": f"dp{n}: one batch of {args.batch} utterances split by utterance over {n} GPU(s) "
-                           "(strong scaling), no collective on the data path",
+                           f"(strong scaling), no collective on the data path; {groups} concurrent stream(s) "
+                           "per GPU, each over its share of the GPU's utterances",
+            "streams_per_gpu": groups,
             "l2": "no flush needed: every step moves "
                   f"{75.6 * max(per) / 64:.1f} GB per GPU through HBM, far more than L2, so no step starts "
                   f"with the previous step's data cached (a stage-2 tensor is {gpu_bytes / 1e6:.0f} MB per GPU)",
-            "launches_per_step": 49}
+            "launches_per_step": 49 * groups}
 
 
 # ---------------------------------------------------------------------------
@@ -535,38 +542,87 @@ def model_hot_nodes(rt, torch):
                     "resident; captured: the same node executions replayed as one CUDA graph"}
 
 
-class RankStream:
-    """One rank's share of the job: its FusedDecoder over `batch` utterances,
-    conv stand-ins drawn on the device, pinned host buffers holding the
-    per-step inputs (features, fc outputs), all seeded per rank."""
+def stream_groups(batch, streams):
+    """Concurrent groups a rank splits its utterances into: `streams`, or by
+    default 2 for 2-32 utterances (measured on one B200: at 8 and 16
+    utterances two concurrent streams run 21 % and 9 % faster, because one
+    group's row staging overlaps the other's statistics and output passes
+    and a launch's partial last wave no longer idles the GPU), else 1."""
+    if streams:
+        return max(1, min(int(streams), batch))
+    return 2 if 2 <= batch <= 32 else 1
 
-    def __init__(self, batch, t0, rank, dev):
+
+class RankStream:
+    """One rank's share of the job: its utterances in `groups` FusedDecoders
+    (each on its own CUDA stream when there are several), conv stand-ins
+    drawn on the device, pinned host buffers holding the per-step inputs
+    (features, fc outputs), all seeded per rank and group."""
+
+    def __init__(self, batch, t0, rank, dev, groups=1):
         from bt_b200.decoder import FusedDecoder, build_stream, fill_conv_standins, host_inputs
         from bt_b200 import shard
         import torch
         self.batch = batch
-        self.S = build_stream(batch, t0=t0)
-        self.dec = FusedDecoder(self.S, dev)
-        fill_conv_standins(self.dec, seed=shard.rank_seed(17, rank))
-        host = host_inputs(self.S, seed=shard.rank_seed(100, rank))
-        self.hin, self.hout = self.dec.host_buffers()
-        self.dec.fill_host(self.hin, host)
-        self.dec.run_host(self.hin, self.hout)             # inputs resident from here on
+        self.parts = []
+        sizes = [batch // groups + (1 if g < batch % groups else 0) for g in range(groups)]
+        for g, b in enumerate(sizes):
+            S = build_stream(b, t0=t0)
+            dec = FusedDecoder(S, dev)
+            fill_conv_standins(dec, seed=shard.rank_seed(17, rank) + 7919 * g)
+            host = host_inputs(S, seed=shard.rank_seed(100, rank) + 7919 * g)
+            hin, hout = dec.host_buffers()
+            dec.fill_host(hin, host)
+            dec.run_host(hin, hout)                        # inputs resident from here on
+            self.parts.append((S, dec, hin, hout))
+        self.streams = [torch.cuda.Stream(dev) for _ in self.parts] if len(self.parts) > 1 else []
         torch.cuda.synchronize()
 
-    def device_steps(self, steps, warmup, barrier, record=None):
-        """Seconds for `steps` launches of the stream (CUDA events on the
+    @property
+    def stages(self):
+        return [S for S, *_ in self.parts]
+
+    def _fan(self, fn):
+        """fn(g, part) for every group: on its own stream when there are
+        several (forked from and joined back into the current stream)."""
+        import torch
+        if not self.streams:
+            return [fn(0, self.parts[0])]
+        main = torch.cuda.current_stream()
+        fork = torch.cuda.Event()
+        fork.record(main)
+        res = []
+        for g, (part, st) in enumerate(zip(self.parts, self.streams)):
+            st.wait_event(fork)
+            with torch.cuda.stream(st):
+                res.append(fn(g, part))
+            join = torch.cuda.Event()
+            join.record(st)
+            main.wait_event(join)
+        return res
+
+    def launch(self, record=None, serial=False):
+        """One step of every group (concurrently unless `serial`); returns
+        the kernel launches."""
+        if serial or not self.streams:
+            return sum(dec.launch(record=record) for _, dec, _, _ in self.parts)
+        return sum(self._fan(lambda g, part: part[1].launch(record=record)))
+
+    def device_steps(self, steps, warmup, barrier, record=None, serial=False):
+        """Seconds for `steps` steps of the stream (CUDA events on the
         launch stream, barrier + synchronize on both sides); returns
-        (seconds, kernel launches)."""
+        (seconds, kernel launches).  With `record`, every launch is also
+        bracketed by CUDA events (run with `serial`: the groups one after
+        the other, so that no two launches overlap)."""
         import torch
         for _ in range(warmup):
-            self.dec.launch()
+            self.launch(serial=serial)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         launches = 0
         for _ in range(steps):
-            launches += self.dec.launch(record=record)
+            launches += self.launch(record=record, serial=serial)
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -579,18 +635,26 @@ class RankStream:
         neighbouring steps' compute); returns (seconds, h2d, d2h bytes per
         step)."""
         import torch
-        pipe = self.dec.host_pipeline(self.hin, self.hout)
+        pipes = [dec.host_pipeline(hin, hout) for _, dec, hin, hout in self.parts]
+
+        def step():
+            moved = self._fan(lambda g, part: pipes[g].step())
+            return sum(m[0] for m in moved), sum(m[1] for m in moved)
+
+        def finish():
+            self._fan(lambda g, part: pipes[g].finish())
+
         for _ in range(warmup):
-            pipe.step()
-        pipe.finish()
+            step()
+        finish()
         torch.cuda.synchronize()
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record()
         h2d = d2h = 0
         for _ in range(steps):
-            h2d, d2h = pipe.step()
-        pipe.finish()
+            h2d, d2h = step()
+        finish()
         f1.record()
         torch.cuda.synchronize()
         barrier()
@@ -598,7 +662,7 @@ class RankStream:
 
     def release(self):
         import torch
-        del self.dec, self.hin, self.hout
+        del self.parts
         torch.cuda.empty_cache()
 
 
@@ -632,7 +696,8 @@ def run_b200(args):
     # this rank's share of the one batch (strong scaling): utterances
     # shard.split_utterances(batch, n, rank), inputs seeded per rank
     _, mine = shard.split_utterances(args.batch, n, rank)
-    rs = RankStream(mine, args.t0, rank, dev)
+    groups = stream_groups(mine, args.streams)
+    rs = RankStream(mine, args.t0, rank, dev, groups)
 
     def barrier():
         shard.barrier(dev)
@@ -643,12 +708,20 @@ def run_b200(args):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    record = []
-    dt, launches = rs.device_steps(args.steps, args.warmup, barrier, record=record)
+    # the timed steps: no event between launches (a pair of CUDA events
+    # around every launch adds a gap after each kernel: 11 % of the step at
+    # 8 utterances per GPU, 2-3 % at 64)
+    dt, launches = rs.device_steps(args.steps, args.warmup, barrier)
     clk = clocks.stop()
     elapsed = max_over_ranks(dt)
     value = args.batch * args.steps / elapsed
     ms_step = 1e3 * elapsed / args.steps
+    # the roofline pass: the same steps again, every launch bracketed by CUDA
+    # events on its stream and the groups run one after the other, so that
+    # each launch's duration is its own
+    record = []
+    rdt, _ = rs.device_steps(args.steps, 1, barrier, record=record, serial=True)
+    roofline_ms_step = 1e3 * max_over_ranks(rdt) / args.steps
 
     # dominant kernel: bt_adain_snake launches of the timed region
     ad_bytes = ad_time = 0.0
@@ -669,8 +742,11 @@ def run_b200(args):
                 "traffic": traffic, "launches_timed": ad_n,
                 "algorithmic_bytes_per_launch": round(ad_bytes / max(ad_n, 1)),
                 "avg_launch_ms": round(1e3 * ad_time / max(ad_n, 1), 4),
-                "share_of_step_time": round(ad_time / max(sum(kind_time.values()), 1e-12), 4)}
-    stream_bytes = stream_algorithmic_bytes(rs.S)
+                "share_of_step_time": round(ad_time / max(sum(kind_time.values()), 1e-12), 4),
+                "measured": "CUDA events around every launch, in a second pass of the same steps (groups run "
+                            "one after the other) right after the timed one",
+                "pass_ms_per_step": round(roofline_ms_step, 3)}
+    stream_bytes = sum(stream_algorithmic_bytes(S) for S in rs.stages)
     stream_bytes_all = int(shard.sum_over_ranks(stream_bytes, device=dev))
 
     # end to end through the host-buffer API
@@ -696,7 +772,7 @@ def run_b200(args):
     weak = None
     if n > 1 and not args.no_weak:
         rs.release()
-        rw = RankStream(args.weak_batch, args.t0, rank, dev)
+        rw = RankStream(args.weak_batch, args.t0, rank, dev, stream_groups(args.weak_batch, args.streams))
         wdt, _ = rw.device_steps(args.steps, args.warmup, barrier)
         wdt = max_over_ranks(wdt)
         we_dt, _, wd2h = rw.e2e_steps(args.steps, args.warmup, barrier)
@@ -728,7 +804,7 @@ def run_b200(args):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-                "vs_baseline": None, "dtype": "f32", "data": DATA, "config": config(args, n),
+                "vs_baseline": None, "dtype": "f32", "data": DATA, "config": config(args, n, groups),
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "e2e_limit": e2e_limit,
                 "gpu_launches": launches * n, "gpu_launches_per_rank": launches,
                 "clocks": clk, "stream_algorithmic_bytes_per_step": stream_bytes_all,
@@ -866,6 +942,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=64,
                     help="utterances in the batch, split over the GPUs (strong scaling)")
+    ap.add_argument("--streams", type=int, default=0,
+                    help="concurrent decoder streams per GPU (0: 2 for 2-32 utterances per GPU, else 1)")
     ap.add_argument("--weak-batch", type=int, default=64,
                     help="utterances per GPU of the weak-scaling figure reported beside it at N > 1")
     ap.add_argument("--no-weak", action="store_true", help="skip the weak-scaling figure at N > 1")
