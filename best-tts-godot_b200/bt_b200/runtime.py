@@ -463,6 +463,33 @@ class BtRuntime:
                 self._remember(key, plan)
             env[node_output[0]] = out
             return
+        if op in ("ReduceMean", "ReduceSum"):                 # ref :589-598
+            x = env[node_input[0]]
+            ax = env[node_input[1]] if len(node_input) > 1 and node_input[1] else at.get("axes")
+            if type(x) is torch.Tensor and x.is_cuda and not isinstance(ax, torch.Tensor):
+                akey = None if ax is None else tuple(np.asarray(ax).reshape(-1).tolist())
+                key = (op, akey, at.get("keepdims", 1), at.get("noop_with_empty_axes", 0), x.dtype, x.shape,
+                       x.stride())
+                plan = self._node_plans.get(key)
+                if plan is None:
+                    plan = self._reduce_plan(op, x, akey, at)
+                    if plan is not None:
+                        self._remember(key, plan)
+                if plan is not None:
+                    env[node_output[0]] = self._run_reduce_plan(plan, x)
+                    return
+        if op == "Concat":                                    # ref :531-535
+            vals = [env[i] for i in node_input if i]
+            if vals and all(type(v) is torch.Tensor and v.is_cuda for v in vals):
+                key = (op, at["axis"], tuple((v.dtype, v.shape, v.stride()) for v in vals))
+                plan = self._node_plans.get(key)
+                if plan is None:
+                    plan = self._concat_plan(vals, at["axis"])
+                    if plan is not None:
+                        self._remember(key, plan)
+                if plan is not None:
+                    env[node_output[0]] = self._run_concat_plan(plan, vals)
+                    return
 
         def arg(i, default=None):
             if i >= len(node_input) or not node_input[i]:
@@ -813,6 +840,104 @@ class BtRuntime:
         self._stream()
         check(self.lib.bt_reduce(kind, tensor_desc(x), axes, n_axes, 1, tensor_desc(out)), "bt_reduce")
         self.launches += 1
+        return out
+
+    def _reduce_plan(self, op, x, axes, at):
+        """The cached launch of a reduction in its common form: a dense
+        float32 tensor reduced over one contiguous block of axes (one
+        bt_reduce launch, as _reduce runs it).  None for every other case,
+        which _reduce handles (and where it raises, it raises there)."""
+        if np_dtype(x) != np.float32 or not x.is_contiguous() or x.numel() == 0:
+            return None
+        nd = x.dim()
+        if axes is None:
+            if at.get("noop_with_empty_axes", 0):
+                return None
+            axes = tuple(range(nd))
+        if len(axes) == 0 or any(not -nd <= a < nd for a in axes):
+            return None
+        norm = sorted(set(int(a) % nd for a in axes))
+        if len(norm) != len(axes) or any(x.shape[i] == 0 for i in norm):
+            return None
+        blocks = _axis_blocks(norm, x.shape)
+        if len(blocks) != 1:
+            return None
+        blk = blocks[0]
+        keep = bool(at.get("keepdims", 1))
+        kshape = tuple(1 if i in blk else int(s) for i, s in enumerate(x.shape))
+        out_shape = tuple(1 if i in norm else int(s) for i, s in enumerate(x.shape)) if keep else \
+            tuple(int(s) for i, s in enumerate(x.shape) if i not in norm)
+        strides, acc = [], 1
+        for d in reversed(kshape):
+            strides.append(acc)
+            acc *= d
+        od = make_tensor(0, np.dtype(np.float32), kshape, tuple(reversed(strides)))
+        return (1 if op == "ReduceMean" else 0, (ctypes_i64 * len(blk))(*blk), len(blk), tensor_desc(x), od, kshape,
+                out_shape)
+
+    def _run_reduce_plan(self, plan, x):
+        kind, axes, n_axes, xd, od, kshape, out_shape = plan
+        out = torch.empty(kshape, dtype=torch.float32, device=self.device)
+        xd.data = x.data_ptr()
+        od.data = out.data_ptr()
+        lib = self.lib
+        lib.bt_set_stream(_raw_stream(self._index))   # always BT_OK
+        rc = lib.bt_reduce(kind, xd, axes, n_axes, 1, od)
+        if rc:
+            check(rc, "bt_reduce")
+        self.launches += 1
+        return out.reshape(out_shape)
+
+    def _concat_plan(self, vals, axis):
+        """The cached launches of a Concat whose inputs need no widening:
+        the result's layout and, per non-empty input, the copy into its
+        slice (descriptors prepared once).  None for every other case, which
+        concat handles (and where it raises, it raises there)."""
+        if any(v.dtype == torch.float16 for v in vals):
+            return None
+        nd = vals[0].dim()
+        axis = int(axis)
+        if not -nd <= axis < nd:
+            return None
+        axis %= nd
+        for v in vals[1:]:
+            if v.dim() != nd or any(v.shape[d] != vals[0].shape[d] for d in range(nd) if d != axis):
+                return None
+        dt = np.result_type(*[np_dtype(v) for v in vals])
+        shape = [int(s) for s in vals[0].shape]
+        shape[axis] = sum(int(v.shape[axis]) for v in vals)
+        strides, acc = [], 1
+        for d in reversed(shape):
+            strides.append(acc)
+            acc *= d
+        strides = tuple(reversed(strides))
+        item = np.dtype(dt).itemsize
+        copies, off = [], 0
+        for i, v in enumerate(vals):
+            n = int(v.shape[axis])
+            if n:
+                part = list(shape)
+                part[axis] = n
+                cdt = self._copy_compute(np.result_type(np_dtype(v), dt))
+                copies.append((i, (_lib.BtTensor * 1)(tensor_desc(v)), make_tensor(0, np.dtype(dt), part, strides),
+                               _lib.BtEwAttrs(_lib.NP_TO_BT[np.dtype(cdt)], 0.0), off * strides[axis] * item))
+            off += n
+        return tuple(shape), NP_TO_TORCH[np.dtype(dt)], copies
+
+    def _run_concat_plan(self, plan, vals):
+        shape, tdt, copies = plan
+        out = torch.empty(shape, dtype=tdt, device=self.device)
+        if copies:
+            base = out.data_ptr()
+            lib = self.lib
+            lib.bt_set_stream(_raw_stream(self._index))   # always BT_OK
+            for i, descs, od, attrs, offb in copies:
+                descs[0].data = vals[i].data_ptr()
+                od.data = base + offb
+                rc = lib.bt_elementwise(OP["IDENTITY"], 1, descs, od, attrs)
+                if rc:
+                    check(rc, "bt_elementwise(concat)")
+                self.launches += 1
         return out
 
     def _mean_from_sum(self, s, count):
