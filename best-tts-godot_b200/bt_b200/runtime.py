@@ -479,8 +479,10 @@ class BtRuntime:
                     env[node_output[0]] = self._run_reduce_plan(plan, x)
                     return
         if op == "Concat":                                    # ref :531-535
-            vals = [env[i] for i in node_input if i]
-            if vals and all(type(v) is torch.Tensor and v.is_cuda for v in vals):
+            # (host values -- the model's shape arithmetic -- are uploaded once
+            # and cached by to_device)
+            vals = [self.to_device(env[i]) for i in node_input if i]
+            if vals and all(type(v) is torch.Tensor for v in vals):
                 key = (op, at["axis"], tuple((v.dtype, v.shape, v.stride()) for v in vals))
                 plan = self._node_plans.get(key)
                 if plan is None:
