@@ -206,11 +206,6 @@ __device__ __forceinline__ float div_row_fast(float a, float b, float y) {
 __device__ __forceinline__ bool div_row_outside(float a, const RowDiv& d) {
   return (f_bits(a) & 0x7f800000u) - kRowDivLo >= d.span;
 }
-// RN(a / b) for any a: the fast form inside the window, div_by with
-// rb = recip_d(b) outside (callers form rb only where some value needs it)
-__device__ __forceinline__ float div_row(float a, const RowDiv& d, double rb) {
-  return div_row_outside(a, d) ? div_by(a, rb) : div_row_fast(a, d.b, d.y);
-}
 #endif
 
 // ---------------------------------------------------------------------------
